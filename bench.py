@@ -1,0 +1,428 @@
+"""Benchmark: bs=1 Llama-3.2-1B greedy decode on B200 through the megakernel.
+
+Workload: seeded random-init Llama-3.2-1B in bf16, a
+128-token seeded prompt (fed through the decode kernel one position per
+launch, untimed), then greedy decode steps from position 128 on, max context
+1024. One step = one launch of the persistent kernel = all 16 layers + final
+norm + lm_head + argmax for one token; the argmax feeds the next launch on the
+device (no host round trip). ``value`` = tokens/s over the K timed steps
+(CUDA events on the launching stream), max over ranks.
+
+``e2e`` runs the same steps through the public API
+(``MegakernelLlamaForCausalLM.forward`` with a pinned host token and
+position, H2D copy, launch, D2H of the next id, host sync per step).
+
+``roofline``: algorithmic bytes per step (2,471,632,896 B of weights + 32,768 B
+per cached position read + 32,768 B of K/V written) / average step time,
+against the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+
+``--impl reference``: the reference's PyTorch Llama path (HF
+``LlamaForCausalLM``, via oracle/) timed on the host CPU cores on a bounded
+sample of the same workload; rank 0 only.
+
+Multi-GPU (torchrun, N > 1): N independent replicas, one per GPU (weak
+scaling); ``value`` = total tokens/s of all ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "bs=1 decode tok/s & p50 token latency at ctx 1024; % of 8 TB/s HBM roofline"
+PROMPT_LEN = 128
+MAX_CTX = 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=640)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-sweep", action="store_true", help="skip the ctx sweep extra")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--small", action="store_true",
+                    help="profiling case: a few steps, no e2e / sweep / cpu baseline")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
+def traffic_summary():
+    p = ROOT / "profiles" / "decode_kernel_traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("dram_bytes_per_launch")
+    return None
+
+
+# ----------------------------------------------------------------------------
+# CPU: the reference's PyTorch path (HF Llama) on the host cores
+# ----------------------------------------------------------------------------
+
+def cpu_reference(weights_cpu, seconds: float, ctx: int = 448):
+    """HF LlamaForCausalLM decode steps on CPU at context ~ctx (the workload's
+    mean context: 128 prompt + 640 steps / 2). Returns (tok/s, detail)."""
+    from transformers import DynamicCache
+
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+    from oracle import llama_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = O.hf_model(cfg, weights_cpu)
+    k, v = syn.random_kv_rows(cfg, ctx, seed=7)
+    cache = DynamicCache(config=model.config)
+    for l in range(cfg.num_layers):
+        cache.update(k[l:l + 1].clone(), v[l:l + 1].clone(), l)
+    tok = int(syn.random_tokens(1, cfg.vocab, seed=9)[0])
+    times = []
+    with torch.no_grad():
+        t_end = time.perf_counter() + seconds
+        pos = ctx
+        while time.perf_counter() < t_end or len(times) < 3:
+            t0 = time.perf_counter()
+            out = model(input_ids=torch.tensor([[tok]]), position_ids=torch.tensor([[pos]]),
+                        past_key_values=cache, use_cache=True)
+            tok = int(out.logits[0, -1].argmax())
+            times.append(time.perf_counter() - t0)
+            pos += 1
+    steps = len(times) - 1  # first step warms the allocator
+    tps = steps / sum(times[1:])
+    cpu = "unknown"
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                cpu = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return tps, {"cores": threads, "cpu_model": cpu, "steps": steps, "ctx_start": ctx,
+                 "p50_ms": statistics.median(times[1:]) * 1e3}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+
+    w = syn.make_weights(cfg, seed=0, device="cuda" if torch.cuda.is_available() else "cpu")
+    w = {k: t.cpu() for k, t in w.items()}
+    tps, det = cpu_reference(w, args.cpu_seconds)
+    sample = (f"HF LlamaForCausalLM (reference's PyTorch Llama path) bf16 on CPU, "
+              f"{det['steps']} greedy decode steps from ctx {det['ctx_start']}, "
+              f"{det['cores']} threads, {det['cpu_model']}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": det["steps"], "warmup": 1,
+        "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
+        "config": {"workload": "Llama-3.2-1B bs=1 greedy decode (sample at ctx ~448)",
+                   "global_batch": 1, "seq_len": MAX_CTX, "parallelism": "cpu"},
+        "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": det["cores"], "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "p50_ms": det["p50_ms"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# GPU: the megakernel
+# ----------------------------------------------------------------------------
+
+def run_ours(args, ws, rank, local):
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+    from llama1b_megakernel_b200.model import MegakernelLlamaForCausalLM
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hbm_peak, peak_kind = peaks()
+    sweep = not (args.no_sweep or args.small)
+    max_seq = 8192 + 64 if sweep else MAX_CTX
+    w = syn.make_weights(cfg, seed=0, device=dev)
+    model = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=max_seq, page_size=64,
+                                       device=dev)
+    w_cpu = None
+    if rank == 0 and ws == 1 and not (args.no_cpu_baseline or args.small):
+        w_cpu = {k: t.cpu() for k, t in w.items()}
+    del w
+    torch.cuda.empty_cache()
+
+    prompt = syn.random_tokens(PROMPT_LEN, cfg.vocab, seed=1).reshape(1, -1)
+    kv = model.kv
+    out = model.forward(prompt, past_key_values=kv, return_logits=False)
+
+    # ------------------------------------------------------------ device loop
+    K, W = args.steps, args.warmup
+    if PROMPT_LEN + K > MAX_CTX:
+        raise SystemExit(f"--steps must keep the context within {MAX_CTX}")
+    kv.reserve(0, MAX_CTX)
+    tok = torch.empty(1, dtype=torch.int32, device=dev)
+    pos = torch.empty(1, dtype=torch.int32, device=dev)
+    nxt = torch.empty(1, dtype=torch.int32, device=dev)
+    first_tok = out.next_ids.to(torch.int32)
+
+    def reset():
+        tok.copy_(first_tok)
+        pos.fill_(PROMPT_LEN)
+
+    reset()
+    for _ in range(W):
+        model.launch(tok, pos, kv, None, nxt, feedback=True)
+    model.sync()
+    reset()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    clocks = ClockSampler(local)
+    barrier(ws)
+    clocks.start()
+    torch.cuda.synchronize()
+    for i in range(K):
+        starts[i].record()
+        model.launch(tok, pos, kv, None, nxt, feedback=True)
+        ends[i].record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    clk = clocks.stop()
+    model.sync()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = starts[0].elapsed_time(ends[-1])
+    total_ms = max_over_ranks(total_ms, ws)
+    tokens_all = K * ws
+    value = tokens_all / (total_ms / 1e3)
+    p50 = statistics.median(step_ms)
+    p90 = sorted(step_ms)[int(0.9 * (K - 1))]
+    p99 = sorted(step_ms)[int(0.99 * (K - 1))]
+    kernel_ms = statistics.mean(step_ms)
+    ctx_mean = PROMPT_LEN + (K - 1) / 2.0
+    bytes_step = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_position() * ctx_mean + \
+        cfg.kv_bytes_per_position()
+    achieved = bytes_step / (kernel_ms / 1e3) / 1e9
+
+    # ------------------------------------------------------------ e2e (public API)
+    e2e_val = None
+    h2d = d2h = 0
+    if not args.small:
+        n = min(args.e2e_steps, MAX_CTX - PROMPT_LEN)
+        kv2 = model.new_cache(max_seq_len=max_seq)
+        model.forward(prompt, past_key_values=kv2, return_logits=False)
+        ids = torch.empty(1, 1, dtype=torch.int32).pin_memory()
+        ps = torch.empty(1, 1, dtype=torch.int32).pin_memory()
+        ids[0, 0] = int(first_tok[0])
+        kv2.reserve(0, PROMPT_LEN + n + 1)
+        for i in range(3):  # warm-up on the same cache positions
+            ps[0, 0] = PROMPT_LEN + i
+            model.forward(ids, ps, past_key_values=kv2, return_logits=False)
+        ids[0, 0] = int(first_tok[0])
+        barrier(ws)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n):
+            ps[0, 0] = PROMPT_LEN + i
+            o = model.forward(ids, ps, past_key_values=kv2, return_logits=False)
+            ids[0, 0] = int(o.next_ids[0])  # D2H of the result, host feeds it back
+        t1 = time.perf_counter()
+        e2e_s = max_over_ranks(t1 - t0, ws)
+        e2e_val = n * ws / e2e_s
+        h2d = 2 * 4   # token id + position (int32) per step
+        d2h = 4       # next id (int32) per step
+
+    # ------------------------------------------------------------ ctx sweep
+    sweep_res = None
+    if sweep:
+        sweep_res = {}
+        for L in (128, 1024, 4096, 8192):
+            kv3 = model.new_cache(max_seq_len=max_seq, num_pages=kv.num_pages)
+            k, v = syn.random_kv_rows(cfg, L, seed=L, device=dev)
+            kv3.fill(0, k, v)
+            kv3.reserve(0, L + 1)
+            del k, v
+            t_ = torch.tensor([7], dtype=torch.int32, device=dev)
+            p_ = torch.tensor([L], dtype=torch.int32, device=dev)
+            for _ in range(3):
+                model.launch(t_, p_, kv3, None, nxt)
+            model.sync()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(21)]
+            ev[0].record()
+            for j in range(20):
+                model.launch(t_, p_, kv3, None, nxt)
+                ev[j + 1].record()
+            torch.cuda.synchronize()
+            model.sync()
+            ms = [ev[j].elapsed_time(ev[j + 1]) for j in range(20)]
+            med = statistics.median(ms)
+            b = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_position() * (L + 1)
+            sweep_res[str(L)] = {"ms_p50": med, "tok_s": 1e3 / med,
+                                 "achieved_gbs": b / (med / 1e3) / 1e9,
+                                 "frac_of_peak": b / (med / 1e3) / 1e9 / hbm_peak}
+            del kv3
+            torch.cuda.empty_cache()
+
+    # ------------------------------------------------------------ cpu baseline
+    cpu_b = None
+    if w_cpu is not None:
+        del model
+        torch.cuda.empty_cache()
+        tps, det = cpu_reference(w_cpu, args.cpu_seconds)
+        cpu_b = {"value": tps, "unit": "tok/s", "cores": det["cores"], "kind": "port",
+                 "sample": (f"HF LlamaForCausalLM (the reference's PyTorch Llama path, via "
+                            f"oracle/) bf16, {det['steps']} decode steps from ctx "
+                            f"{det['ctx_start']} on {det['cpu_model']}")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K,
+            "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, seeded random prompt)",
+            "config": {"workload": "Llama-3.2-1B bs=1 greedy decode: 128-token prompt, then "
+                                   f"{K} steps from position 128 (max ctx 1024)",
+                       "global_batch": ws, "seq_len": MAX_CTX, "parallelism": f"replicas x{ws}",
+                       "l2": "inputs larger than L2 (2.47 GB of weights streamed per step)"},
+            "p50_ms": p50, "p90_ms": p90, "p99_ms": p99,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_kind": peak_kind, "traffic": traffic_summary(),
+                         "bytes_per_step": bytes_step},
+            "frac_of_8tbs": achieved / 8000.0,
+            "clocks": clk,
+            "gpu_launches": K,
+            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+        }
+        if sweep_res is not None:
+            line["ctx_sweep"] = sweep_res
+        if cpu_b is not None:
+            line["cpu_baseline"] = cpu_b
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_init()
+    try:
+        if args.impl == "reference":
+            run_reference(args, ws, rank)
+        else:
+            run_ours(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

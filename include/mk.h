@@ -1,0 +1,169 @@
+/*
+ * mk.h — C ABI of the B200 (sm_100a) Llama decode megakernel.
+ *
+ * One persistent, cooperative CUDA launch decodes one token for every sequence
+ * of a batch: all decoder layers (RMSNorm -> QKV -> llama3 RoPE -> paged KV
+ * scatter -> split-K GQA flash-decode -> o_proj + residual -> RMSNorm ->
+ * SwiGLU gate/up -> down + residual), then the final RMSNorm, the tied lm_head
+ * GEMV and a greedy argmax.
+ *
+ * Ownership: the caller owns every device buffer passed in (weights, KV pages,
+ * block tables, tokens, positions, outputs). The library only borrows the raw
+ * pointers for the duration of a call. Scratch the kernel needs between its
+ * phases (residual, q/k/v, attention partials, barrier counters) is owned by
+ * the MkModel handle and allocated in mk_init.
+ *
+ * Errors: every entry point returns an MkStatus; mk_last_error() gives the
+ * message for the calling thread's last failure. Device-side failures (a
+ * barrier or pipeline wait that ran out of time, a position or page id out of
+ * range) are recorded in a device error word and reported by mk_sync().
+ *
+ * Threading: one stream per handle; calls on one handle are not re-entrant.
+ * mk_decode is asynchronous with respect to the host.
+ *
+ * Reference interfaces this replaces (keaganchern/llama1B-megakernel):
+ *   - transformer_llama_megakernel_16layers(X, Wq, Wk, Wv, Wo, gpre, Wgu, Wd,
+ *     gpost, K_00..K_15, V_00..V_15, cos, sin, position_ids) -> (Y, K.., V..)
+ *     transformer_llama.py:196-237, called at llama_with_megakernel.py:165-173
+ *     -> mk_decode_hidden (hidden in, hidden out, caches updated in place) and
+ *        mk_decode (embedding ... argmax, the whole token-generation step).
+ *   - NeuronLlamaForCausalLMMK.convert_hf_to_neuron_state_dict
+ *     llama_with_megakernel.py:281-351 (pre-stacked weights bound once)
+ *     -> mk_load_weights.
+ *   - the shape/TP asserts at llama_with_megakernel.py:145-162 -> MK_EINVAL
+ *     from mk_init / mk_load_weights / mk_decode.
+ */
+#ifndef MK_H_
+#define MK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum MkStatus {
+  MK_OK = 0,
+  MK_EINVAL = 1,     /* bad argument, shape or configuration */
+  MK_ECUDA = 2,      /* a CUDA runtime call failed */
+  MK_ETIMEOUT = 3,   /* a device-side wait ran out of time; the kernel returned */
+  MK_ENOMEM = 4,     /* device allocation failed */
+  MK_ESTATE = 5,     /* call out of order (e.g. decode before load_weights) */
+  MK_EDEVICE = 6     /* device reported a bad position, page id or token */
+} MkStatus;
+
+/* Model + cache geometry. head_dim must be 64; num_q_heads / num_kv_heads == 4. */
+typedef struct MkConfig {
+  int32_t num_layers;
+  int32_t hidden;
+  int32_t intermediate;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t vocab;
+  float rms_eps;
+  int32_t max_batch;           /* 1..4 */
+  int32_t page_size;           /* KV positions per page, multiple of 8 */
+  int32_t num_pages;           /* pages per layer in the KV pool */
+  int32_t max_blocks_per_seq;  /* columns of the block table */
+  int32_t rope_len;            /* rows of the cos/sin tables (max position + 1) */
+} MkConfig;
+
+/*
+ * Device pointers to the packed bf16 weights (layouts produced by the host
+ * packer, llama1b_megakernel_b200/weights.py):
+ *   embed      [vocab][hidden]                  (also the tied lm_head)
+ *   w_qkv      [L][(nq + 2*nkv) * 32][2][hidden] RoPE pairs: rows (d, d+32) of
+ *                                                each q/k/v head, adjacent
+ *   w_o        [L][hidden][nq * 64]             (HF o_proj.weight)
+ *   w_gate_up  [L][intermediate][2][hidden]     gate row i, up row i adjacent
+ *   w_down     [L][hidden][intermediate]        (HF down_proj.weight)
+ *   norm_attn  [L][hidden], norm_mlp [L][hidden], norm_final [hidden]
+ *   rope_cos, rope_sin [rope_len][64]           bf16 cos/sin per position
+ * All pointers must be 16-byte aligned.
+ */
+typedef struct MkWeights {
+  const void* embed;
+  const void* w_qkv;
+  const void* w_o;
+  const void* w_gate_up;
+  const void* w_down;
+  const void* norm_attn;
+  const void* norm_mlp;
+  const void* norm_final;
+  const void* rope_cos;
+  const void* rope_sin;
+} MkWeights;
+
+/*
+ * Paged bf16 KV cache, updated in place:
+ *   k_pages, v_pages  [L][num_pages][nkv][page_size][64]
+ *   block_tables      [batch][max_blocks_per_seq] int32 page ids (all layers)
+ * Position p of sequence b is slot p % page_size of page
+ * block_tables[b][p / page_size].
+ */
+typedef struct MkKVCache {
+  void* k_pages;
+  void* v_pages;
+  const int32_t* block_tables;
+} MkKVCache;
+
+/* mk_decode flags */
+#define MK_FLAG_FEEDBACK 1  /* after the step: tokens[b] = next id, positions[b] += 1 */
+
+typedef struct MkModel MkModel;
+
+/* Validate cfg, pick the grid for `device`, allocate scratch. */
+int mk_init(const MkConfig* cfg, int device, MkModel** out);
+
+/* Bind (borrow) the packed weight pointers. */
+int mk_load_weights(MkModel* m, const MkWeights* w);
+
+/*
+ * Enqueue one decode step on `stream` (a cudaStream_t, NULL = legacy default).
+ * tokens[batch], positions[batch] (int32, device): the token at `positions[b]`
+ * of sequence b; its K/V row is written at that position. logits (device,
+ * [batch][vocab] fp32) may be NULL. next_ids (device, [batch] int32) gets the
+ * greedy argmax (lowest index on ties).
+ */
+int mk_decode(MkModel* m, const int32_t* tokens, const int32_t* positions, int32_t batch,
+              const MkKVCache* kv, float* logits, int32_t* next_ids, int32_t flags,
+              void* stream);
+
+/*
+ * The decoder layers only, the role of the reference's 16-layer kernel:
+ * hidden_in [batch][hidden] bf16 (the embedded token) -> hidden_out
+ * [batch][hidden] bf16 (the residual after the last layer, before the final
+ * norm); KV rows written at positions like mk_decode.
+ */
+int mk_decode_hidden(MkModel* m, const void* hidden_in, const int32_t* positions, int32_t batch,
+                     const MkKVCache* kv, void* hidden_out, void* stream);
+
+/* Wait for `stream`, then report and clear any device-side error. */
+int mk_sync(MkModel* m, void* stream);
+
+/* Device-side wait limit in nanoseconds (default 2e9). */
+int mk_set_timeout_ns(MkModel* m, uint64_t ns);
+
+/*
+ * Test knob for failure detection: CTA `cta` skips its arrival at the first
+ * grid barrier of the next launches (-1 disables), so every other CTA's wait
+ * runs out and the launch ends with MK_ETIMEOUT instead of hanging.
+ */
+int mk_debug_skip_arrival(MkModel* m, int32_t cta);
+
+/* Launch geometry chosen by mk_init: CTAs (one per SM) and ring slots per CTA. */
+int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem_bytes);
+
+/* Last error message of the calling thread ("" if none). */
+const char* mk_last_error(void);
+
+/* Free scratch and the handle. */
+int mk_destroy(MkModel* m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MK_H_ */

@@ -1,0 +1,398 @@
+// mk_api.cu — C ABI (include/mk.h) around the persistent decode megakernel.
+//
+// The handle owns the inter-phase scratch (residual, q/k/v, attention
+// partials, barrier counters, argmax keys, the device error word); everything
+// else is borrowed from the caller per call. Launches are cooperative so all
+// CTAs (one per SM) are co-resident, which the kernel's grid barriers need.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/mk.h"
+#include "mk_kernel.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define MK_CUDA(call)                                                                    \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess) return fail(MK_ECUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+struct MkModel {
+  MkConfig cfg;
+  int device = 0;
+  int num_sms = 0;
+  int grid = 0;
+  int num_slots = 0;
+  int smem = 0;
+  int kmax = 0;
+  bool has_weights = false;
+  MkWeights w{};
+  unsigned long long timeout_ns = 2000000000ull;
+  int debug_skip_cta = -1;
+  // scratch
+  void* scratch = nullptr;
+  mk::bf16* h = nullptr;
+  mk::bf16* qkv = nullptr;
+  mk::bf16* attn = nullptr;
+  mk::bf16* act = nullptr;
+  float* partials = nullptr;
+  uint32_t* counters = nullptr;
+  unsigned long long* keys = nullptr;
+  int* error = nullptr;
+  int* host_error = nullptr;      // mapped pinned mirror, read by mk_sync
+  int* host_error_dev = nullptr;  // its device address
+  size_t counters_bytes = 0;
+};
+
+namespace {
+
+int validate_config(const MkConfig* c) {
+  if (!c) return fail(MK_EINVAL, "config is NULL");
+  if (c->num_layers <= 0) return fail(MK_EINVAL, "num_layers must be > 0");
+  if (c->head_dim != 64) return fail(MK_EINVAL, "head_dim must be 64 (got %d)", c->head_dim);
+  if (c->num_kv_heads <= 0 || c->num_q_heads != 4 * c->num_kv_heads)
+    return fail(MK_EINVAL, "num_q_heads must be 4 * num_kv_heads (got %d, %d)", c->num_q_heads,
+                c->num_kv_heads);
+  if (c->hidden <= 0 || c->hidden % 256 || c->hidden > 4096)
+    return fail(MK_EINVAL, "hidden must be a multiple of 256 in [256, 4096] (got %d)", c->hidden);
+  if (c->intermediate <= 0 || c->intermediate % 256 || c->intermediate > 8192)
+    return fail(MK_EINVAL, "intermediate must be a multiple of 256 in [256, 8192] (got %d)",
+                c->intermediate);
+  if ((c->num_q_heads * 64) % 256 || c->num_q_heads * 64 > 8192)
+    return fail(MK_EINVAL, "num_q_heads * 64 must be a multiple of 256, <= 8192");
+  if (c->vocab <= 0) return fail(MK_EINVAL, "vocab must be > 0");
+  if (!(c->rms_eps > 0.f)) return fail(MK_EINVAL, "rms_eps must be > 0");
+  if (c->max_batch < 1 || c->max_batch > 4)
+    return fail(MK_EINVAL, "max_batch must be in [1, 4] (got %d)", c->max_batch);
+  if (c->page_size < 8 || c->page_size % 8)
+    return fail(MK_EINVAL, "page_size must be a positive multiple of 8 (got %d)", c->page_size);
+  if (c->num_pages <= 0 || c->max_blocks_per_seq <= 0)
+    return fail(MK_EINVAL, "num_pages and max_blocks_per_seq must be > 0");
+  if (c->rope_len <= 0) return fail(MK_EINVAL, "rope_len must be > 0");
+  return MK_OK;
+}
+
+template <int B>
+cudaError_t launch_b(const mk::Params& p, int grid, int smem, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(mk::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mk::decode_kernel<B>, p);
+}
+
+template <int B>
+cudaError_t set_smem_b(int smem) {
+  return cudaFuncSetAttribute(mk::decode_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              smem);
+}
+
+template <int B>
+cudaError_t occupancy_b(int* blocks, int smem) {
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, mk::decode_kernel<B>, mk::kThreads,
+                                                       smem);
+}
+
+cudaError_t dispatch_launch(int B, const mk::Params& p, int grid, int smem, cudaStream_t s) {
+  switch (B) {
+    case 1: return launch_b<1>(p, grid, smem, s);
+    case 2: return launch_b<2>(p, grid, smem, s);
+    case 3: return launch_b<3>(p, grid, smem, s);
+    case 4: return launch_b<4>(p, grid, smem, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* positions, int32_t batch,
+            const MkKVCache* kv, const void* hidden_in, void* hidden_out, float* logits,
+            int32_t* next_ids, int32_t flags, void* stream) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (!m->has_weights) return fail(MK_ESTATE, "mk_load_weights has not been called");
+  if (batch < 1 || batch > m->cfg.max_batch)
+    return fail(MK_EINVAL, "batch %d outside [1, max_batch=%d]", batch, m->cfg.max_batch);
+  if (!positions) return fail(MK_EINVAL, "positions is NULL");
+  if (!kv || !kv->k_pages || !kv->v_pages || !kv->block_tables)
+    return fail(MK_EINVAL, "KV cache pointers must be non-NULL");
+  if (!aligned16(kv->k_pages) || !aligned16(kv->v_pages))
+    return fail(MK_EINVAL, "KV page pools must be 16-byte aligned");
+  if (mode == 0) {
+    if (!tokens || !next_ids) return fail(MK_EINVAL, "tokens and next_ids must be non-NULL");
+  } else {
+    if (!hidden_in || !hidden_out) return fail(MK_EINVAL, "hidden_in and hidden_out must be non-NULL");
+    if (!aligned16(hidden_in)) return fail(MK_EINVAL, "hidden_in must be 16-byte aligned");
+  }
+  MK_CUDA(cudaSetDevice(m->device));
+  const MkConfig& c = m->cfg;
+  mk::Params p{};
+  p.L = c.num_layers;
+  p.H = c.hidden;
+  p.I = c.intermediate;
+  p.NQ = c.num_q_heads;
+  p.NKV = c.num_kv_heads;
+  p.V = c.vocab;
+  p.eps = c.rms_eps;
+  p.B = batch;
+  p.page_size = c.page_size;
+  p.num_pages = c.num_pages;
+  p.max_blocks = c.max_blocks_per_seq;
+  p.rope_len = c.rope_len;
+  p.num_slots = m->num_slots;
+  p.kmax = m->kmax;
+  p.mode = mode;
+  p.flags = flags;
+  p.embed = static_cast<const mk::bf16*>(m->w.embed);
+  p.w_qkv = static_cast<const mk::bf16*>(m->w.w_qkv);
+  p.w_o = static_cast<const mk::bf16*>(m->w.w_o);
+  p.w_gu = static_cast<const mk::bf16*>(m->w.w_gate_up);
+  p.w_down = static_cast<const mk::bf16*>(m->w.w_down);
+  p.norm_attn = static_cast<const mk::bf16*>(m->w.norm_attn);
+  p.norm_mlp = static_cast<const mk::bf16*>(m->w.norm_mlp);
+  p.norm_final = static_cast<const mk::bf16*>(m->w.norm_final);
+  p.rope_cos = static_cast<const mk::bf16*>(m->w.rope_cos);
+  p.rope_sin = static_cast<const mk::bf16*>(m->w.rope_sin);
+  p.k_pages = static_cast<mk::bf16*>(kv->k_pages);
+  p.v_pages = static_cast<mk::bf16*>(kv->v_pages);
+  p.block_tables = kv->block_tables;
+  p.tokens = const_cast<int*>(tokens);
+  p.positions = const_cast<int*>(positions);
+  p.hidden_in = static_cast<const mk::bf16*>(hidden_in);
+  p.hidden_out = static_cast<mk::bf16*>(hidden_out);
+  p.logits = logits;
+  p.next_ids = next_ids;
+  p.h = m->h;
+  p.qkv = m->qkv;
+  p.attn = m->attn;
+  p.act = m->act;
+  p.partials = m->partials;
+  p.counters = m->counters;
+  p.keys = m->keys;
+  p.error = m->error;
+  p.host_error = m->host_error_dev;
+  p.timeout_ns = m->timeout_ns;
+  p.debug_skip_cta = m->debug_skip_cta;
+  MK_CUDA(dispatch_launch(batch, p, m->grid, m->smem, static_cast<cudaStream_t>(stream)));
+  return MK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mk_init(const MkConfig* cfg, int device, MkModel** out) {
+  if (!out) return fail(MK_EINVAL, "out is NULL");
+  *out = nullptr;
+  int rc = validate_config(cfg);
+  if (rc) return rc;
+  MK_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  MK_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(MK_EINVAL, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                prop.major, prop.minor);
+  if (!prop.cooperativeLaunch) return fail(MK_EINVAL, "device lacks cooperative launch");
+  MkModel* m = new MkModel();
+  m->cfg = *cfg;
+  m->device = device;
+  m->num_sms = prop.multiProcessorCount;
+  m->kmax = cfg->hidden;
+  if (cfg->intermediate > m->kmax) m->kmax = cfg->intermediate;
+  if (cfg->num_q_heads * 64 > m->kmax) m->kmax = cfg->num_q_heads * 64;
+  const int B = cfg->max_batch;
+  const int smem_cap = (int)prop.sharedMemPerBlockOptin;
+  int slots = 0;
+  for (int s = 16; s >= 4; --s) {
+    if (mk::smem_bytes_for(s, B, m->kmax) <= smem_cap) {
+      slots = s;
+      break;
+    }
+  }
+  if (!slots) {
+    delete m;
+    return fail(MK_EINVAL, "activation rows (%d x %d) leave no room for the ring", B, m->kmax);
+  }
+  m->num_slots = slots;
+  m->smem = mk::smem_bytes_for(slots, B, m->kmax);
+  for (int b = 1; b <= 4; ++b) {
+    cudaError_t e = cudaSuccess;
+    switch (b) {
+      case 1: e = set_smem_b<1>(m->smem); break;
+      case 2: e = set_smem_b<2>(m->smem); break;
+      case 3: e = set_smem_b<3>(m->smem); break;
+      case 4: e = set_smem_b<4>(m->smem); break;
+    }
+    if (e != cudaSuccess) {
+      delete m;
+      return fail(MK_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
+  }
+  int blocks = 0;
+  cudaError_t e = occupancy_b<1>(&blocks, m->smem);
+  if (e != cudaSuccess || blocks < 1) {
+    delete m;
+    return fail(MK_ECUDA, "kernel does not fit one CTA per SM (%s)", cudaGetErrorString(e));
+  }
+  m->grid = m->num_sms;
+
+  // Scratch: one allocation, 256-byte aligned sub-buffers.
+  const size_t H = cfg->hidden, I = cfg->intermediate, NQ = cfg->num_q_heads,
+               NKV = cfg->num_kv_heads;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_h = take(B * H * 2);
+  const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 2);
+  const size_t o_attn = take(B * NQ * 64 * 2);
+  const size_t o_act = take(B * I * 2);
+  const size_t o_part = take(B * NKV * mk::kMaxSplit * mk::kGroup * mk::kPartialStride * 4);
+  const size_t o_cnt = take((mk::kCntArrive + B * NKV) * 4);
+  const size_t o_keys = take(B * 8);
+  const size_t o_err = take(16);
+  m->counters_bytes = o_err + 256 - o_cnt;  // counters, keys and error word
+  void* base = nullptr;
+  e = cudaMalloc(&base, off);
+  if (e != cudaSuccess) {
+    delete m;
+    return fail(MK_ENOMEM, "cudaMalloc(%zu): %s", off, cudaGetErrorString(e));
+  }
+  m->scratch = base;
+  char* cb = static_cast<char*>(base);
+  m->h = reinterpret_cast<mk::bf16*>(cb + o_h);
+  m->qkv = reinterpret_cast<mk::bf16*>(cb + o_qkv);
+  m->attn = reinterpret_cast<mk::bf16*>(cb + o_attn);
+  m->act = reinterpret_cast<mk::bf16*>(cb + o_act);
+  m->partials = reinterpret_cast<float*>(cb + o_part);
+  m->counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
+  m->keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
+  m->error = reinterpret_cast<int*>(cb + o_err);
+  e = cudaMemset(base, 0, off);
+  if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&m->host_error), 16, cudaHostAllocMapped);
+  if (e == cudaSuccess) {
+    memset(m->host_error, 0, 16);
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&m->host_error_dev), m->host_error, 0);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (m->host_error) cudaFreeHost(m->host_error);
+    cudaFree(base);
+    delete m;
+    return fail(MK_ECUDA, "scratch init: %s", cudaGetErrorString(e));
+  }
+  *out = m;
+  return MK_OK;
+}
+
+int mk_load_weights(MkModel* m, const MkWeights* w) {
+  if (!m || !w) return fail(MK_EINVAL, "NULL argument");
+  const void* ptrs[] = {w->embed, w->w_qkv, w->w_o, w->w_gate_up, w->w_down,
+                        w->norm_attn, w->norm_mlp, w->norm_final, w->rope_cos, w->rope_sin};
+  const char* names[] = {"embed", "w_qkv", "w_o", "w_gate_up", "w_down",
+                         "norm_attn", "norm_mlp", "norm_final", "rope_cos", "rope_sin"};
+  for (int i = 0; i < 10; ++i) {
+    if (!ptrs[i]) return fail(MK_EINVAL, "weight pointer %s is NULL", names[i]);
+    if (!aligned16(ptrs[i])) return fail(MK_EINVAL, "weight pointer %s is not 16-byte aligned", names[i]);
+  }
+  m->w = *w;
+  m->has_weights = true;
+  return MK_OK;
+}
+
+int mk_decode(MkModel* m, const int32_t* tokens, const int32_t* positions, int32_t batch,
+              const MkKVCache* kv, float* logits, int32_t* next_ids, int32_t flags, void* stream) {
+  return enqueue(m, 0, tokens, positions, batch, kv, nullptr, nullptr, logits, next_ids, flags,
+                 stream);
+}
+
+int mk_decode_hidden(MkModel* m, const void* hidden_in, const int32_t* positions, int32_t batch,
+                     const MkKVCache* kv, void* hidden_out, void* stream) {
+  return enqueue(m, 1, nullptr, positions, batch, kv, hidden_in, hidden_out, nullptr, nullptr, 0,
+                 stream);
+}
+
+int mk_sync(MkModel* m, void* stream) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  MK_CUDA(cudaSetDevice(m->device));
+  MK_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  volatile int* he = m->host_error;
+  if (he[0] == 0) return MK_OK;
+  int err[4] = {he[0], he[1], he[2], he[3]};
+  // Reset the counters, argmax keys and error words so the next launch starts clean.
+  MK_CUDA(cudaMemset(m->counters, 0, m->counters_bytes));
+  MK_CUDA(cudaDeviceSynchronize());
+  he[0] = he[1] = he[2] = he[3] = 0;
+  const char* what = "unknown";
+  int code = MK_EDEVICE;
+  switch (err[0]) {
+    case mk::kErrBarrierTimeout: what = "grid barrier wait timed out"; code = MK_ETIMEOUT; break;
+    case mk::kErrRingTimeout: what = "weight-stream wait timed out"; code = MK_ETIMEOUT; break;
+    case mk::kErrPosition: what = "position out of range (rope table or block table)"; break;
+    case mk::kErrPage: what = "block table holds a page id outside the pool"; break;
+    case mk::kErrToken: what = "token id outside the vocabulary"; break;
+  }
+  return fail(code, "device error: %s (code %d, detail %d, cta %d, thread %d)", what, err[0],
+              err[1], err[2], err[3]);
+}
+
+int mk_set_timeout_ns(MkModel* m, uint64_t ns) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (ns == 0) return fail(MK_EINVAL, "timeout must be > 0");
+  m->timeout_ns = ns;
+  return MK_OK;
+}
+
+int mk_debug_skip_arrival(MkModel* m, int32_t cta) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  m->debug_skip_cta = cta;
+  return MK_OK;
+}
+
+int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem_bytes) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (grid) *grid = m->grid;
+  if (ring_slots) *ring_slots = m->num_slots;
+  if (smem_bytes) *smem_bytes = m->smem;
+  return MK_OK;
+}
+
+const char* mk_last_error(void) { return g_last_error.c_str(); }
+
+int mk_destroy(MkModel* m) {
+  if (!m) return MK_OK;
+  cudaSetDevice(m->device);
+  if (m->scratch) cudaFree(m->scratch);
+  if (m->host_error) cudaFreeHost(m->host_error);
+  delete m;
+  return MK_OK;
+}
+
+}  // extern "C"

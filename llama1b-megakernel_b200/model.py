@@ -1,0 +1,226 @@
+"""PyTorch module around the decode megakernel.
+
+``MegakernelLlamaForCausalLM`` plays the role of the reference's
+``NeuronLlamaForCausalLMMK`` (llama_with_megakernel.py:355): it owns the packed
+weights (converted once, like ``convert_hf_to_neuron_state_dict``,
+llama_with_megakernel.py:281-351), and its ``forward`` runs decode steps with
+the same inputs an HF/NxDI causal LM takes during token generation —
+``input_ids``, ``position_ids`` and ``past_key_values`` — returning fp32
+logits, the greedy next ids and the (in-place updated) cache.
+
+Every step is one launch of the persistent kernel through the C ABI; there is
+no CPU or PyTorch fallback: without a CUDA device or without libmk.so the
+constructor raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .config import LlamaDecodeConfig
+from .kv_cache import PagedKVCache
+from .weights import PackedWeights, pack_weights
+
+
+@dataclass
+class DecodeOutput:
+    logits: torch.Tensor | None   # [B, V] fp32 (last step), or None
+    next_ids: torch.Tensor        # [B] int64 greedy ids of the last step
+    past_key_values: PagedKVCache
+
+
+class MegakernelLlamaForCausalLM(torch.nn.Module):
+    def __init__(self, cfg: LlamaDecodeConfig, state_dict: dict, max_batch: int = 1,
+                 max_seq_len: int = 2048, page_size: int = 64, device="cuda",
+                 rope_len: int | None = None):
+        super().__init__()
+        if not torch.cuda.is_available():
+            raise RuntimeError("MegakernelLlamaForCausalLM needs a CUDA device (sm_100a)")
+        cfg.validate()
+        self.lib = _lib.load()
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.max_batch = max_batch
+        self.max_seq_len = max_seq_len
+        self.page_size = page_size
+        self.rope_len = rope_len or max_seq_len
+        with torch.cuda.device(self.device):
+            self.packed: PackedWeights = pack_weights(cfg, state_dict, self.rope_len, self.device)
+            self.kv = PagedKVCache(cfg, max_batch, max_seq_len, page_size, device=self.device)
+            self._tokens = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
+            self._positions = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
+            self._next = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
+            self._logits = torch.empty(max_batch, cfg.vocab, dtype=torch.float32, device=self.device)
+        self._handle = ctypes.c_void_p()
+        c = _lib.MkConfig(
+            num_layers=cfg.num_layers, hidden=cfg.hidden, intermediate=cfg.intermediate,
+            num_q_heads=cfg.num_q_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+            vocab=cfg.vocab, rms_eps=cfg.rms_eps, max_batch=max_batch, page_size=page_size,
+            num_pages=self.kv.num_pages, max_blocks_per_seq=self.kv.max_blocks,
+            rope_len=self.rope_len)
+        _lib.check(self.lib.mk_init(ctypes.byref(c), self.device.index, ctypes.byref(self._handle)))
+        pw = self.packed
+        self._weights = _lib.MkWeights(
+            embed=pw.embed.data_ptr(), w_qkv=pw.w_qkv.data_ptr(), w_o=pw.w_o.data_ptr(),
+            w_gate_up=pw.w_gate_up.data_ptr(), w_down=pw.w_down.data_ptr(),
+            norm_attn=pw.norm_attn.data_ptr(), norm_mlp=pw.norm_mlp.data_ptr(),
+            norm_final=pw.norm_final.data_ptr(), rope_cos=pw.rope_cos.data_ptr(),
+            rope_sin=pw.rope_sin.data_ptr())
+        _lib.check(self.lib.mk_load_weights(self._handle, ctypes.byref(self._weights)))
+
+    # ------------------------------------------------------------------ misc
+    def __del__(self):
+        h = getattr(self, "_handle", None)
+        if h is not None and h.value:
+            self.lib.mk_destroy(h)
+            self._handle = ctypes.c_void_p()
+
+    def new_cache(self, max_seq_len: int | None = None, num_pages: int | None = None) -> PagedKVCache:
+        """A fresh cache with this model's geometry (same pool size unless given)."""
+        return PagedKVCache(self.cfg, self.max_batch, max_seq_len or self.max_seq_len,
+                            self.page_size, num_pages or self.kv.num_pages, device=self.device)
+
+    def query(self) -> dict:
+        g, s, m = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        _lib.check(self.lib.mk_query(self._handle, ctypes.byref(g), ctypes.byref(s), ctypes.byref(m)))
+        return {"grid": g.value, "ring_slots": s.value, "smem_bytes": m.value}
+
+    def set_timeout_ns(self, ns: int) -> None:
+        _lib.check(self.lib.mk_set_timeout_ns(self._handle, int(ns)))
+
+    def debug_skip_arrival(self, cta: int) -> None:
+        _lib.check(self.lib.mk_debug_skip_arrival(self._handle, int(cta)))
+
+    def _kv_struct(self, kv: PagedKVCache) -> _lib.MkKVCache:
+        if kv.num_pages > self.kv.num_pages or kv.max_blocks != self.kv.max_blocks \
+                or kv.page_size != self.page_size:
+            raise ValueError("cache geometry differs from the one the model was initialised with")
+        return _lib.MkKVCache(k_pages=kv.k_pages.data_ptr(), v_pages=kv.v_pages.data_ptr(),
+                              block_tables=kv.block_tables.data_ptr())
+
+    @staticmethod
+    def _stream_ptr(stream) -> int:
+        s = stream if stream is not None else torch.cuda.current_stream()
+        return s.cuda_stream
+
+    # ------------------------------------------------------------ low level
+    def launch(self, tokens: torch.Tensor, positions: torch.Tensor, kv: PagedKVCache,
+               logits: torch.Tensor | None, next_ids: torch.Tensor, feedback: bool = False,
+               stream=None) -> None:
+        """Enqueue one step (device int32 tensors, no host sync, no page allocation)."""
+        B = positions.numel()
+        kvs = self._kv_struct(kv)
+        _lib.check(self.lib.mk_decode(
+            self._handle, tokens.data_ptr(), positions.data_ptr(), B, ctypes.byref(kvs),
+            logits.data_ptr() if logits is not None else None, next_ids.data_ptr(),
+            _lib.MK_FLAG_FEEDBACK if feedback else 0, self._stream_ptr(stream)))
+
+    def launch_hidden(self, hidden_in: torch.Tensor, positions: torch.Tensor, kv: PagedKVCache,
+                      hidden_out: torch.Tensor, stream=None) -> None:
+        """Enqueue the decoder layers only: hidden_in [B, H] bf16 -> hidden_out [B, H] bf16."""
+        B = positions.numel()
+        kvs = self._kv_struct(kv)
+        _lib.check(self.lib.mk_decode_hidden(
+            self._handle, hidden_in.data_ptr(), positions.data_ptr(), B, ctypes.byref(kvs),
+            hidden_out.data_ptr(), self._stream_ptr(stream)))
+
+    def sync(self, stream=None) -> None:
+        """Wait for the stream and raise ``MkError`` if the device reported one."""
+        _lib.check(self.lib.mk_sync(self._handle, self._stream_ptr(stream)))
+
+    # ------------------------------------------------------------ model API
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, position_ids: torch.Tensor | None = None,
+                past_key_values: PagedKVCache | None = None, return_logits: bool = True,
+                sync: bool = True) -> DecodeOutput:
+        """Run ``input_ids`` [B, T] through the model one position at a time.
+
+        ``position_ids`` [B, T] default to each sequence's current length.
+        K/V rows are written at those positions of ``past_key_values`` (the
+        model's own cache when None). Returns the last step's fp32 logits
+        [B, V], its greedy ids [B] and the cache.
+        """
+        kv = past_key_values if past_key_values is not None else self.kv
+        ids = torch.as_tensor(input_ids)
+        if ids.dim() == 1:
+            ids = ids[None, :]
+        B, T = ids.shape
+        if B > self.max_batch:
+            raise ValueError(f"batch {B} > max_batch {self.max_batch}")
+        if position_ids is None:
+            start = torch.tensor(kv.seq_lens[:B], dtype=torch.int64)
+            position_ids = start[:, None] + torch.arange(T)[None, :]
+        pos = torch.as_tensor(position_ids).reshape(B, T)
+        pos_host = pos.cpu()
+        for b in range(B):
+            kv.reserve(b, int(pos_host[b].max()) + 1)
+        ids_dev = ids.to(device=self.device, dtype=torch.int32, non_blocking=True)
+        pos_dev = pos.to(device=self.device, dtype=torch.int32, non_blocking=True)
+        logits = self._logits[:B] if return_logits else None
+        for t in range(T):
+            tok = ids_dev[:, t].contiguous()
+            ps = pos_dev[:, t].contiguous()
+            self.launch(tok, ps, kv, logits if t == T - 1 else None, self._next[:B])
+        for b in range(B):
+            kv.seq_lens[b] = max(kv.seq_lens[b], int(pos_host[b].max()) + 1)
+        if sync:
+            self.sync()
+        return DecodeOutput(logits.clone() if logits is not None else None,
+                            self._next[:B].to(torch.int64), kv)
+
+    @torch.no_grad()
+    def forward_hidden(self, hidden: torch.Tensor, position_ids: torch.Tensor,
+                       past_key_values: PagedKVCache | None = None) -> torch.Tensor:
+        """The decoder layers only (the reference kernel's X -> Y): [B, H] -> [B, H]."""
+        kv = past_key_values if past_key_values is not None else self.kv
+        h = hidden.reshape(-1, self.cfg.hidden).to(self.device, torch.bfloat16).contiguous()
+        B = h.shape[0]
+        pos = torch.as_tensor(position_ids).reshape(B)
+        for b in range(B):
+            kv.reserve(b, int(pos[b]) + 1)
+        pos_dev = pos.to(device=self.device, dtype=torch.int32)
+        out = torch.empty_like(h)
+        self.launch_hidden(h, pos_dev, kv, out)
+        for b in range(B):
+            kv.seq_lens[b] = max(kv.seq_lens[b], int(pos[b]) + 1)
+        self.sync()
+        return out
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int,
+                 past_key_values: PagedKVCache | None = None) -> torch.Tensor:
+        """Greedy decoding: feed the prompt, then ``max_new_tokens`` steps on device.
+
+        The prompt goes through the decode kernel one position per launch.
+        The generated steps run back to back without host round trips: each
+        launch writes its argmax into the next launch's token slot and bumps
+        the position (MK_FLAG_FEEDBACK). Returns [B, max_new_tokens] int64.
+        """
+        kv = past_key_values if past_key_values is not None else self.kv
+        ids = torch.as_tensor(input_ids)
+        if ids.dim() == 1:
+            ids = ids[None, :]
+        B, T = ids.shape
+        out = self.forward(ids, past_key_values=kv, return_logits=False, sync=True)
+        start = torch.tensor(kv.seq_lens[:B], dtype=torch.int32)
+        for b in range(B):
+            kv.reserve(b, int(start[b]) + max_new_tokens)
+        tok = self._tokens[:B]
+        pos = self._positions[:B]
+        tok.copy_(out.next_ids.to(torch.int32))
+        pos.copy_(start.to(self.device))
+        result = torch.empty(B, max_new_tokens, dtype=torch.int32, device=self.device)
+        result[:, 0] = tok
+        for s in range(1, max_new_tokens):
+            self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
+            result[:, s] = tok
+        self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
+        self.sync()
+        for b in range(B):
+            kv.seq_lens[b] = int(start[b]) + max_new_tokens
+        return result.to(torch.int64)
