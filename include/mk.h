@@ -153,6 +153,22 @@ int mk_set_timeout_ns(MkModel* m, uint64_t ns);
  */
 int mk_debug_skip_arrival(MkModel* m, int32_t cta);
 
+/*
+ * Phase trace, off by default (no counterpart in the reference; it plays the
+ * role of the reference's profiler captures, main.py:377-407). With a device
+ * buffer of at least *needed uint64 entries, every later launch records, per
+ * CTA and per phase, globaltimer stamps and stall totals:
+ *   buffer[(cta * (num_layers * 5 + 1) + phase) * 8 + kind]
+ *   phase = layer * 5 + {0 QKV, 1 attention, 2 o_proj, 3 gate/up, 4 down},
+ *           num_layers * 5 = lm_head;
+ *   kind  = 0 wait start, 1 wait passed, 2 activations loaded, 3 phase done,
+ *           4 consumer ns stalled on the weight stream (cumulative),
+ *           5 first copy issued, 6 producer ns stalled on a full ring
+ *           (cumulative), 7 last copy issued.
+ * buffer NULL switches tracing off; *needed (may be NULL) is set either way.
+ */
+int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed);
+
 /* Launch geometry chosen by mk_init: CTAs (one per SM) and ring slots per CTA. */
 int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem_bytes);
 

@@ -64,7 +64,14 @@ struct MkModel {
   int* host_error = nullptr;      // mapped pinned mirror, read by mk_sync
   int* host_error_dev = nullptr;  // its device address
   size_t counters_bytes = 0;
+  unsigned long long* trace = nullptr;  // borrowed, see mk_set_trace
 };
+
+namespace {
+int64_t trace_entries(const MkModel* m) {
+  return (int64_t)m->grid * (m->cfg.num_layers * 5 + 1) * mk::kTraceKinds;
+}
+}  // namespace
 
 namespace {
 
@@ -198,6 +205,8 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   p.host_error = m->host_error_dev;
   p.timeout_ns = m->timeout_ns;
   p.debug_skip_cta = m->debug_skip_cta;
+  p.trace = m->trace;
+  p.trace_per_cta = (c.num_layers * 5 + 1) * mk::kTraceKinds;
   MK_CUDA(dispatch_launch(batch, p, m->grid, m->smem, static_cast<cudaStream_t>(stream)));
   return MK_OK;
 }
@@ -373,6 +382,22 @@ int mk_set_timeout_ns(MkModel* m, uint64_t ns) {
 int mk_debug_skip_arrival(MkModel* m, int32_t cta) {
   if (!m) return fail(MK_EINVAL, "model is NULL");
   m->debug_skip_cta = cta;
+  return MK_OK;
+}
+
+int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  const int64_t n = trace_entries(m);
+  if (needed) *needed = n;
+  if (!buffer) {
+    m->trace = nullptr;
+    return MK_OK;
+  }
+  if (capacity < n)
+    return fail(MK_EINVAL, "trace buffer holds %lld entries, a launch writes %lld",
+                (long long)capacity, (long long)n);
+  if (reinterpret_cast<uintptr_t>(buffer) & 7) return fail(MK_EINVAL, "trace buffer must be 8-byte aligned");
+  m->trace = reinterpret_cast<unsigned long long*>(buffer);
   return MK_OK;
 }
 

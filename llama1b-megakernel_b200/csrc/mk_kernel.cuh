@@ -93,7 +93,29 @@ struct Params {
   int* host_error;           // [4] mapped pinned host mirror of `error`
   unsigned long long timeout_ns;
   int debug_skip_cta;
+  // optional phase trace ([grid][trace_per_cta] u64, see kTrace*); nullptr = off
+  unsigned long long* trace;
+  int trace_per_cta;
 };
+
+// Phase trace. Phase index: layer * 5 + {0 QKV, 1 ATTN, 2 O, 3 GU, 4 DOWN},
+// num_layers * 5 = LM head. Per (CTA, phase) kTraceKinds u64 entries:
+enum TraceKind : int {
+  kTrWaitStart = 0,    // consumers reach the phase's grid wait (globaltimer ns)
+  kTrWaitDone = 1,     // wait passed
+  kTrRowsLoaded = 2,   // activation rows in shared memory (normalised)
+  kTrDone = 3,         // consumers finished the phase
+  kTrConsStall = 4,    // cumulative ns warp 0 waited for ring data, at phase end
+  kTrProdStart = 5,    // producer issues the phase's first copy
+  kTrProdStall = 6,    // cumulative ns the producer waited for a free slot
+  kTrProdEnd = 7,      // producer issued the phase's last copy
+  kTraceKinds = 8,
+};
+
+__device__ __forceinline__ void trace_put(const Params& p, int phase, int kind,
+                                          unsigned long long v) {
+  if (p.trace) p.trace[(size_t)blockIdx.x * p.trace_per_cta + phase * kTraceKinds + kind] = v;
+}
 
 struct SmemState {
   int tok[4];
@@ -233,6 +255,7 @@ struct Ring {
   uint64_t* empty;
   int S;
   uint32_t n = 0;  // fills seen so far (same count on both sides)
+  unsigned long long stall_ns = 0;  // time spent waiting (traced runs only)
 };
 
 // Consumer warp: wait for fill n; nullptr on abort/timeout. Every lane waits
@@ -244,6 +267,7 @@ __device__ __noinline__ const uint8_t* ring_wait(const Params& p, Ring& r, int w
   uint64_t* bar = &r.full[slot];
   bool done = mbar_try_wait(bar, parity);
   uint64_t t0 = 0;
+  const uint64_t ts = (p.trace && !__all_sync(0xffffffffu, done)) ? global_ns() : 0;
   for (uint32_t it = 0; !__all_sync(0xffffffffu, done); ++it) {
     if (!done) done = mbar_try_wait(bar, parity);
     int give_up = 0;
@@ -259,6 +283,7 @@ __device__ __noinline__ const uint8_t* ring_wait(const Params& p, Ring& r, int w
     }
     if (__shfl_sync(0xffffffffu, give_up, 0)) return nullptr;
   }
+  if (ts) r.stall_ns += global_ns() - ts;
   return r.slots + (size_t)slot * kSlotBytes;
 }
 
@@ -282,10 +307,12 @@ struct Producer {
     const int slot = r.n % r.S;
     if (r.n >= (uint32_t)r.S) {
       const uint32_t parity = ((r.n / r.S) + 1) & 1;
+      const uint64_t ts = p.trace ? global_ns() : 0;
       if (!mbar_wait(p, &r.empty[slot], parity, 100, p.timeout_ns)) {
         ok = false;
         return nullptr;
       }
+      if (ts) r.stall_ns += global_ns() - ts;
     }
     mbar_arrive_expect_tx(&r.full[slot], bytes);
     return r.slots + (size_t)slot * kSlotBytes;
@@ -354,19 +381,42 @@ __device__ void run_producer(const Params& p, const SmemState& st, Ring& ring) {
   const int NQKV = p.NQ + 2 * p.NKV;
   const int H = p.H, I = p.I, QD = p.NQ * kHeadDim;
   const int T = B * p.NKV * st.n_split;
+  auto mark = [&](int ph, bool start) {
+    if (!p.trace) return;
+    if (start) {
+      trace_put(p, ph, kTrProdStart, global_ns());
+    } else {
+      trace_put(p, ph, kTrProdEnd, global_ns());
+      trace_put(p, ph, kTrProdStall, ring.stall_ns);
+    }
+  };
   for (int l = 0; l < p.L && pr.ok; ++l) {
+    mark(l * 5 + 0, true);
     pr.units(p.w_qkv + (size_t)l * NQKV * 32 * 2 * H, 4 * H, sch.next(NQKV * 32));
+    mark(l * 5 + 0, false);
+    mark(l * 5 + 1, true);
     for (int it = blockIdx.x; it < T && pr.ok; it += gridDim.x) {
       const AttnItem a = attn_item(p, st, it);
       for (int c0 = a.p0; c0 < a.p1 && pr.ok; c0 += kAttnChunk) {
         pr.kv_chunk(l, a.b, a.g, c0, min(kAttnChunk, a.p1 - c0));
       }
     }
+    mark(l * 5 + 1, false);
+    mark(l * 5 + 2, true);
     pr.units(p.w_o + (size_t)l * H * QD, 2 * QD, sch.next(H));
+    mark(l * 5 + 2, false);
+    mark(l * 5 + 3, true);
     pr.units(p.w_gu + (size_t)l * I * 2 * H, 4 * H, sch.next(I));
+    mark(l * 5 + 3, false);
+    mark(l * 5 + 4, true);
     pr.units(p.w_down + (size_t)l * H * I, 2 * I, sch.next(H));
+    mark(l * 5 + 4, false);
   }
-  if (p.mode == 0 && pr.ok) pr.units(p.embed, 2 * H, sch.next(p.V));
+  if (p.mode == 0 && pr.ok) {
+    mark(p.L * 5, true);
+    pr.units(p.embed, 2 * H, sch.next(p.V));
+    mark(p.L * 5, false);
+  }
   if (!pr.ok) pr.drain();
 }
 
@@ -698,12 +748,23 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
   uint32_t barriers = 0;  // grid barriers passed so far
   const int G = gridDim.x;
   (void)warp;
+  auto mark = [&](int ph, int kind) {
+    if (p.trace && threadIdx.x == 0) trace_put(p, ph, kind, global_ns());
+  };
+  auto mark_done = [&](int ph) {
+    if (p.trace && threadIdx.x == 0) {
+      trace_put(p, ph, kTrDone, global_ns());
+      trace_put(p, ph, kTrConsStall, ring.stall_ns);
+    }
+  };
 
   for (int l = 0; l < p.L; ++l) {
     // ------------------------------------------------------------- QKV
+    mark(l * 5 + 0, kTrWaitStart);
     if (l > 0) {
       if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 1000 + l)) return;
     }
+    mark(l * 5 + 0, kTrWaitDone);
     {
       const bf16* src[B];
 #pragma unroll
@@ -713,6 +774,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       }
       load_rows<B>(src, H, p.norm_attn + (size_t)l * H, p.eps, xs, p.kmax, st);
     }
+    mark(l * 5 + 0, kTrRowsLoaded);
     const Split sq = sch.next(NQKV * 32);
     const size_t kv_layer = (size_t)l * p.num_pages * p.NKV * p.page_size * kHeadDim;
     bool ok = rows_phase<B, 2>(p, ring, xs, H, sq, 2000 + l, [&](int u, float (&acc)[2][B], int lane) {
@@ -750,22 +812,29 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         }
       }
     });
+    mark_done(l * 5 + 0);
     if (!grid_arrive(p, ok, l == 0 && (int)blockIdx.x == p.debug_skip_cta)) return;
     ++barriers;
 
     // ------------------------------------------------------------- ATTN
+    mark(l * 5 + 1, kTrWaitStart);
     if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 3000 + l)) return;
+    mark(l * 5 + 1, kTrWaitDone);
     if (!attention_phase<B>(p, ring, st, l, comb, qs, kvn)) return;
+    mark_done(l * 5 + 1);
 
     // ------------------------------------------------------------- O
+    mark(l * 5 + 2, kTrWaitStart);
     if (!grid_wait(p, p.counters + kCntHeadsDone, (uint32_t)((l + 1) * B * p.NKV), 4000 + l))
       return;
+    mark(l * 5 + 2, kTrWaitDone);
     {
       const bf16* src[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) src[b] = p.attn + (size_t)b * QD;
       load_rows<B>(src, QD, nullptr, 0.f, xs, p.kmax, st);
     }
+    mark(l * 5 + 2, kTrRowsLoaded);
     ok = rows_phase<B, 1>(p, ring, xs, QD, sch.next(H), 5000 + l, [&](int u, float (&acc)[1][B], int lane) {
 #pragma unroll
       for (int b = 0; b < B; ++b) {
@@ -776,17 +845,21 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         p.h[(size_t)b * H + u] = f2bf(r + rbf(acc[0][b]));
       }
     });
+    mark_done(l * 5 + 2);
     if (!grid_arrive(p, ok, false)) return;
     ++barriers;
 
     // ------------------------------------------------------------- GU
+    mark(l * 5 + 3, kTrWaitStart);
     if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 6000 + l)) return;
+    mark(l * 5 + 3, kTrWaitDone);
     {
       const bf16* src[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) src[b] = p.h + (size_t)b * H;
       load_rows<B>(src, H, p.norm_mlp + (size_t)l * H, p.eps, xs, p.kmax, st);
     }
+    mark(l * 5 + 3, kTrRowsLoaded);
     ok = rows_phase<B, 2>(p, ring, xs, H, sch.next(I), 7000 + l, [&](int u, float (&acc)[2][B], int lane) {
 #pragma unroll
       for (int b = 0; b < B; ++b) {
@@ -797,17 +870,21 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         p.act[(size_t)b * I + u] = f2bf(s * up);
       }
     });
+    mark_done(l * 5 + 3);
     if (!grid_arrive(p, ok, false)) return;
     ++barriers;
 
     // ------------------------------------------------------------- DOWN
+    mark(l * 5 + 4, kTrWaitStart);
     if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 8000 + l)) return;
+    mark(l * 5 + 4, kTrWaitDone);
     {
       const bf16* src[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) src[b] = p.act + (size_t)b * I;
       load_rows<B>(src, I, nullptr, 0.f, xs, p.kmax, st);
     }
+    mark(l * 5 + 4, kTrRowsLoaded);
     const bool last_layer = (l == p.L - 1);
     ok = rows_phase<B, 1>(p, ring, xs, I, sch.next(H), 9000 + l, [&](int u, float (&acc)[1][B], int lane) {
 #pragma unroll
@@ -819,6 +896,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = y;
       }
     });
+    mark_done(l * 5 + 4);
     if (last_layer && p.mode == 1) {
       if (consumer_any(!ok)) return;
     } else {
@@ -829,13 +907,16 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
 
   // --------------------------------------------------------------- LM head
   if (p.mode == 0) {
+    mark(p.L * 5, kTrWaitStart);
     if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 10000)) return;
+    mark(p.L * 5, kTrWaitDone);
     {
       const bf16* src[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) src[b] = p.h + (size_t)b * H;
       load_rows<B>(src, H, p.norm_final, p.eps, xs, p.kmax, st);
     }
+    mark(p.L * 5, kTrRowsLoaded);
     float best_v[B];
     int best_i[B];
 #pragma unroll
@@ -855,6 +936,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       }
     });
     if (consumer_any(!ok)) return;
+    mark_done(p.L * 5);
     const int lane = tid & 31, w = tid >> 5;
     if (lane == 0) {
 #pragma unroll

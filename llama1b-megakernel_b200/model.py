@@ -96,6 +96,22 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
     def debug_skip_arrival(self, cta: int) -> None:
         _lib.check(self.lib.mk_debug_skip_arrival(self._handle, int(cta)))
 
+    def set_trace(self, enable: bool = True) -> torch.Tensor | None:
+        """Record the phase trace of every later launch into a device buffer
+        (int64, [grid, num_layers * 5 + 1, 8]; see ``mk_set_trace``), or stop."""
+        need = ctypes.c_int64()
+        if not enable:
+            _lib.check(self.lib.mk_set_trace(self._handle, None, 0, ctypes.byref(need)))
+            self._trace = None
+            return None
+        _lib.check(self.lib.mk_set_trace(self._handle, None, 0, ctypes.byref(need)))
+        grid = self.query()["grid"]
+        buf = torch.zeros(need.value, dtype=torch.int64, device=self.device)
+        _lib.check(self.lib.mk_set_trace(self._handle, buf.data_ptr(), buf.numel(),
+                                         ctypes.byref(need)))
+        self._trace = buf.view(grid, self.cfg.num_layers * 5 + 1, 8)
+        return self._trace
+
     def _kv_struct(self, kv: PagedKVCache) -> _lib.MkKVCache:
         if kv.num_pages > self.kv.num_pages or kv.max_blocks != self.kv.max_blocks \
                 or kv.page_size != self.page_size:

@@ -96,6 +96,8 @@ class OracleKV:
         ps = self.page_size
         nb = (n + ps - 1) // ps
         pages = self.block_tables[b, :nb].long()
+        if bool((pages < 0).any()):
+            raise IndexError(f"sequence {b}: positions < {n} include unreserved pages")
         k = self.k_pages[layer, pages].permute(1, 0, 2, 3).reshape(self.k_pages.shape[2], nb * ps, -1)
         v = self.v_pages[layer, pages].permute(1, 0, 2, 3).reshape(self.v_pages.shape[2], nb * ps, -1)
         return k[:, :n], v[:, :n]
@@ -104,6 +106,8 @@ class OracleKV:
         """Store K/V rows [nkv, hd] at position ``pos`` of sequence b."""
         ps = self.page_size
         page = int(self.block_tables[b, pos // ps])
+        if page < 0:
+            raise IndexError(f"sequence {b}: position {pos} is in an unreserved page")
         self.k_pages[layer, page, :, pos % ps] = k_row
         self.v_pages[layer, page, :, pos % ps] = v_row
 

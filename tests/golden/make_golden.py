@@ -5,6 +5,7 @@ checkout for the RoPE fixture):
 
     python tests/golden/make_golden.py rope      # rope_llama3.json
     python tests/golden/make_golden.py greedy    # llama1b_greedy640.json (~1 min)
+    python tests/golden/make_golden.py envelope  # adds the fp32 agreement (~20 min)
 
 ``rope``: the reference's own ``Llama3RotaryEmbedding`` class is lifted out of
 its llama.py with ``ast`` (the module itself cannot be imported here: it
@@ -140,6 +141,48 @@ def make_greedy(n_prompt: int = 128, n_steps: int = 640, seed: int = 0, prompt_s
     print("wrote llama1b_greedy640.json")
 
 
+def make_envelope() -> None:
+    """fp32 evaluation of the greedy workload, teacher-forced on the fixture.
+
+    The same decode steps in fp32 arithmetic (weights widened from the same
+    bf16 values, fp32 cache, the same bf16 RoPE table), fed the fixture's own
+    tokens. Its argmax agreement with the bf16 greedy tokens measures how many
+    decisions in this random-init model are within bf16 rounding noise: any
+    correct implementation whose rounding differs from the reference's is
+    expected to agree at about this rate, not at 100%.
+    """
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+    from oracle import llama_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    path = HERE / "llama1b_greedy640.json"
+    d = json.loads(path.read_text())
+    w = {k: v.float() for k, v in syn.make_weights(cfg, seed=0).items()}
+    ps = d["page_size"]
+    n_prompt, n_steps = len(d["prompt"]), len(d["tokens"])
+    nblk = (n_prompt + n_steps + ps - 1) // ps
+    kv = O.OracleKV(
+        torch.zeros(cfg.num_layers, nblk, cfg.num_kv_heads, ps, cfg.head_dim),
+        torch.zeros(cfg.num_layers, nblk, cfg.num_kv_heads, ps, cfg.head_dim),
+        torch.arange(nblk, dtype=torch.int32).reshape(1, -1))
+    inv = O.llama3_inv_freq(cfg)
+    feed = [d["prompt"][-1]] + d["tokens"][:-1]
+    t0 = time.time()
+    ids = []
+    with torch.no_grad():
+        for t in range(n_prompt - 1):
+            O.decode_step(cfg, w, kv, d["prompt"][t:t + 1], [t], inv_freq=inv, layers=cfg.num_layers)
+        for s in range(n_steps):
+            r = O.decode_step(cfg, w, kv, [feed[s]], [n_prompt - 1 + s], inv_freq=inv)
+            ids.append(int(r["next"][0]))
+    match = sum(int(a == b) for a, b in zip(ids, d["tokens"])) / n_steps
+    print(f"fp32 teacher-forced match {match:.4f} ({time.time() - t0:.0f}s)")
+    d["fp32_teacher_forced_match"] = match
+    d["fp32_teacher_forced_ids"] = ids
+    path.write_text(json.dumps(d) + "\n")
+
+
 def refresh_fingerprint() -> None:
     from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
 
@@ -157,3 +200,5 @@ if __name__ == "__main__":
         make_rope()
     if "greedy" in what:
         make_greedy()
+    if "envelope" in what:
+        make_envelope()
