@@ -154,17 +154,28 @@ int mk_set_timeout_ns(MkModel* m, uint64_t ns);
 int mk_debug_skip_arrival(MkModel* m, int32_t cta);
 
 /*
+ * L2 prefetch of the weight stream: each CTA's prefetch lane runs at most
+ * `lead_slots` 16 KB ring fills ahead of its bulk-copy producer, paced so the
+ * whole grid issues `gbytes_per_s` (0 = unpaced); lead_slots 0 turns it off
+ * (the default). No counterpart in the reference (the Neuron compiler
+ * schedules its own DMA prefetch, transformer_llama.py:117-122).
+ */
+int mk_set_prefetch(MkModel* m, int32_t lead_slots, float gbytes_per_s);
+
+/*
  * Phase trace, off by default (no counterpart in the reference; it plays the
  * role of the reference's profiler captures, main.py:377-407). With a device
  * buffer of at least *needed uint64 entries, every later launch records, per
  * CTA and per phase, globaltimer stamps and stall totals:
- *   buffer[(cta * (num_layers * 5 + 1) + phase) * 8 + kind]
+ *   buffer[(cta * (num_layers * 5 + 1) + phase) * 12 + kind]
  *   phase = layer * 5 + {0 QKV, 1 attention, 2 o_proj, 3 gate/up, 4 down},
  *           num_layers * 5 = lm_head;
  *   kind  = 0 wait start, 1 wait passed, 2 activations loaded, 3 phase done,
  *           4 consumer ns stalled on the weight stream (cumulative),
  *           5 first copy issued, 6 producer ns stalled on a full ring
- *           (cumulative), 7 last copy issued.
+ *           (cumulative), 7 last copy issued; attention phases also
+ *           8 q loaded, 9 cached chunks reduced, 10 split arrival counted,
+ *           11 last split merged (for the CTA's last item).
  * buffer NULL switches tracing off; *needed (may be NULL) is set either way.
  */
 int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed);

@@ -6,6 +6,7 @@
 // CTAs (one per SM) are co-resident, which the kernel's grid barriers need.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -47,6 +48,9 @@ struct MkModel {
   int num_slots = 0;
   int smem = 0;
   int kmax = 0;
+  int part_cap = 0;
+  int prefetch_slots = 0;
+  float prefetch_gbs = 0.f;
   bool has_weights = false;
   MkWeights w{};
   unsigned long long timeout_ns = 2000000000ull;
@@ -173,6 +177,12 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   p.rope_len = c.rope_len;
   p.num_slots = m->num_slots;
   p.kmax = m->kmax;
+  p.nseg_h = mk::pieces_per_row(c.hidden);
+  p.nseg_qd = mk::pieces_per_row(c.num_q_heads * 64);
+  p.nseg_i = mk::pieces_per_row(c.intermediate);
+  p.part_cap = m->part_cap;
+  p.prefetch_slots = m->prefetch_slots;
+  p.prefetch_ns_per_byte = m->prefetch_gbs > 0.f ? (float)m->grid / m->prefetch_gbs : 0.f;
   p.mode = mode;
   p.flags = flags;
   p.embed = static_cast<const mk::bf16*>(m->w.embed);
@@ -236,9 +246,21 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   if (cfg->num_q_heads * 64 > m->kmax) m->kmax = cfg->num_q_heads * 64;
   const int B = cfg->max_batch;
   const int smem_cap = (int)prop.sharedMemPerBlockOptin;
+  {
+    // Partial sums one CTA keeps per phase: its most units x pieces per unit.
+    const int G = prop.multiProcessorCount;
+    auto per_cta = [G](int units) { return (units + G - 1) / G; };
+    const int nh = mk::pieces_per_row(cfg->hidden), nqd = mk::pieces_per_row(cfg->num_q_heads * 64),
+              ni = mk::pieces_per_row(cfg->intermediate);
+    int cap = per_cta((cfg->num_q_heads + 2 * cfg->num_kv_heads) * 32) * 2 * nh;
+    cap = std::max(cap, per_cta(cfg->hidden) * nqd);
+    cap = std::max(cap, per_cta(cfg->intermediate) * 2 * nh);
+    cap = std::max(cap, per_cta(cfg->hidden) * ni);
+    m->part_cap = cap * B;
+  }
   int slots = 0;
   for (int s = 16; s >= 4; --s) {
-    if (mk::smem_bytes_for(s, B, m->kmax) <= smem_cap) {
+    if (mk::smem_bytes_for(s, B, m->kmax, m->part_cap, cfg->hidden) <= smem_cap) {
       slots = s;
       break;
     }
@@ -248,7 +270,7 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
     return fail(MK_EINVAL, "activation rows (%d x %d) leave no room for the ring", B, m->kmax);
   }
   m->num_slots = slots;
-  m->smem = mk::smem_bytes_for(slots, B, m->kmax);
+  m->smem = mk::smem_bytes_for(slots, B, m->kmax, m->part_cap, cfg->hidden);
   for (int b = 1; b <= 4; ++b) {
     cudaError_t e = cudaSuccess;
     switch (b) {
@@ -269,6 +291,12 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
     return fail(MK_ECUDA, "kernel does not fit one CTA per SM (%s)", cudaGetErrorString(e));
   }
   m->grid = m->num_sms;
+  // The o_proj prologue keeps one (m, l) pair per attention item (at most one
+  // item per CTA, four heads each) in the attention scratch.
+  if (8 * m->grid * 4 > mk::kAttnWarps * mk::kGroup * mk::kPartialStride * 4) {
+    delete m;
+    return fail(MK_EINVAL, "grid of %d CTAs exceeds the attention scratch", m->grid);
+  }
 
   // Scratch: one allocation, 256-byte aligned sub-buffers.
   const size_t H = cfg->hidden, I = cfg->intermediate, NQ = cfg->num_q_heads,
@@ -382,6 +410,16 @@ int mk_set_timeout_ns(MkModel* m, uint64_t ns) {
 int mk_debug_skip_arrival(MkModel* m, int32_t cta) {
   if (!m) return fail(MK_EINVAL, "model is NULL");
   m->debug_skip_cta = cta;
+  return MK_OK;
+}
+
+int mk_set_prefetch(MkModel* m, int32_t lead_slots, float gbytes_per_s) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (lead_slots < 0 || lead_slots > 4096)
+    return fail(MK_EINVAL, "prefetch lead %d outside [0, 4096]", lead_slots);
+  if (!(gbytes_per_s >= 0.f)) return fail(MK_EINVAL, "prefetch rate must be >= 0");
+  m->prefetch_slots = lead_slots;
+  m->prefetch_gbs = gbytes_per_s;
   return MK_OK;
 }
 

@@ -14,11 +14,16 @@ namespace mk {
 constexpr int kHeadDim = 64;
 constexpr int kGroup = 4;                  // q heads per kv head
 constexpr int kSlotBytes = 16384;          // one ring slot
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
+constexpr int kAttnWarps = 8;              // consumer warps that work on attention chunks
+constexpr int kProducerWarp = kConsumerWarps;      // lane 0 issues the ring copies
+constexpr int kPrefetchWarp = kConsumerWarps + 1;  // lane 0 issues L2 prefetches ahead of it
+constexpr int kThreads = kConsumerThreads + 64;
+constexpr int kSegCols = 2048;             // max columns of one piece (a row segment)
 constexpr int kAttnChunk = 64;             // cached positions per attention slot
 constexpr int kMaxSplit = 32;              // split-K pieces per (sequence, kv head)
+constexpr int kSplitMinPositions = 64;     // no split shorter than this (one chunk)
 constexpr int kPartialStride = kHeadDim + 2;  // o[64], m, l per q head
 
 // Device error codes (error word [0]).
@@ -112,6 +117,28 @@ __device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint
       : "memory");
 }
 
+// Warm L2 with [src, src + bytes) without waiting (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 128-bit shared-memory load at a shared-window address. volatile: it must stay
+// after the mbarrier wait that made the bulk-copied bytes visible.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+// mbarrier arrive counting `count` arrivals at once.
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(count)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- global sync
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
@@ -122,6 +149,14 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
 
 __device__ __forceinline__ void red_release_add_u32(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Atomic add with acquire+release semantics at GPU scope (arrival counters
+// whose last arriver reads what the others wrote).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_u32(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ int ld_volatile_i32(const int* p) {
@@ -158,6 +193,19 @@ __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }
 // Round to bf16 and back: the value a bf16 tensor op would store.
 __device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// c0 += lo(a) * lo(b), c1 += hi(a) * hi(b) for packed bf16 pairs, in fp32:
+// the products of two bf16 values are exact in fp32, so this equals an fp32
+// FMA of the widened operands.
+__device__ __forceinline__ void fma2_bf16(uint32_t a, uint32_t b, float& c0, float& c1) {
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\t"
+      "mov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+      "fma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "r"(a), "r"(b));
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

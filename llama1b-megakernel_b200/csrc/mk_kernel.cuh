@@ -4,7 +4,7 @@
 // sequences through every decoder layer, then the final norm, the tied
 // lm_head and a greedy argmax.
 //
-// CTA = 8 consumer warps + 1 producer warp.
+// CTA = 16 consumer warps + 1 producer warp + 1 prefetch warp.
 //
 // * The producer (one lane) walks the CTA's whole schedule of HBM reads for
 //   the step — its slice of every weight matrix of every layer, its KV-cache
@@ -12,14 +12,21 @@
 //   (cp.async.bulk, the TMA engine without a tensor map) into a ring of 16 KB
 //   shared-memory slots, each guarded by a full/empty mbarrier pair. Weights
 //   and cached K/V do not depend on activations, so the producer never waits
-//   for a grid barrier: it runs ahead by the ring's depth (~190 KB per SM) and
-//   keeps HBM busy while the consumers sit in phase barriers.
-// * The consumers walk the same schedule. Each phase starts by reading the
-//   activation vector it needs (bf16 residual, q/k/v, attention output or the
-//   SwiGLU product, all L2-resident) into shared memory, RMS-normalising it
-//   where the layer does, then reduces each streamed weight row against it
-//   (one warp per row or row pair, fp32 accumulation, warp-shuffle reduction)
-//   and writes the phase output.
+//   for a grid barrier: it runs ahead by the ring's depth (~190 KB per SM).
+// * The prefetch lane walks the same schedule a configurable number of slots
+//   ahead of the producer and warms L2 with cp.async.bulk.prefetch.L2, so the
+//   stream keeps HBM busy through grid barriers and the attention phase, and
+//   the producer refills freed slots from L2.
+// * The consumers walk the same schedule. Every streamed row is cut into
+//   pieces of at most 2048 columns (4 KB); piece q of a phase goes to warp
+//   q mod 16, so each slot is read by four warps at once, each with 128-bit
+//   shared loads. A warp keeps its 2048-column segment of the activation
+//   vector in registers as packed bf16 and accumulates with mixed-precision
+//   fma.rn.f32.bf16 into four independent fp32 chains, then reduces across
+//   the warp and leaves one fp32 partial per piece in shared memory. After
+//   the phase the partials of each output are summed in a fixed order and
+//   the epilogue (RoPE, KV scatter, SiLU*up, residual add) runs one thread
+//   per output, off the streaming loop.
 //
 // Phases per layer (grid barrier = acquire/release counter, time-bounded):
 //   QKV    RMSNorm(h), q/k/v rows in RoPE pairs (d, d+32), llama3 RoPE from a
@@ -59,6 +66,10 @@ struct Params {
   int kmax;  // max(H, I, NQ*64): stride of the activation rows in shared memory
   int mode;  // 0: full step (embedding .. argmax); 1: decoder layers only
   int flags;
+  int nseg_h, nseg_qd, nseg_i;  // pieces per row for K = H, NQ*64, I
+  int part_cap;                 // floats in the shared partial-sum array
+  int prefetch_slots;           // L2 prefetch lead over the producer, in slots (0 = off)
+  float prefetch_ns_per_byte;   // pacing of the L2 prefetch (0 = unpaced)
   // weights (packed, see mk.h)
   const bf16* embed;
   const bf16* w_qkv;
@@ -109,7 +120,11 @@ enum TraceKind : int {
   kTrProdStart = 5,    // producer issues the phase's first copy
   kTrProdStall = 6,    // cumulative ns the producer waited for a free slot
   kTrProdEnd = 7,      // producer issued the phase's last copy
-  kTraceKinds = 8,
+  kTrAttnQ = 8,        // attention: q / new K,V loaded (last item of the CTA)
+  kTrAttnChunks = 9,   // attention: cached chunks reduced
+  kTrAttnArrive = 10,  // attention: split partials written, arrival counted
+  kTrAttnMerged = 11,  // attention: last split merged and published (if last)
+  kTraceKinds = 12,
 };
 
 __device__ __forceinline__ void trace_put(const Params& p, int phase, int kind,
@@ -122,22 +137,33 @@ struct SmemState {
   int pos[4];
   int n_split;
   int flag;
-  int pad[6];
+  uint32_t prod_fills;  // ring fills the producer has issued (read by the prefetch lane)
+  int pad[5];
   float red[kConsumerWarps * 4];
   float am_val[kConsumerWarps * 4];
   int am_idx[kConsumerWarps * 4];
 };
 
 // Shared-memory layout (dynamic): [ring S x 16 KB][x rows B x kmax bf16]
+// [partials part_cap fp32][raw residual B x H bf16][RoPE rows B x 128 bf16]
 // [attention scratch][mbarriers 2 x S][SmemState]
 constexpr int kAttnScratchBytes =
-    kConsumerWarps * kGroup * kPartialStride * 4 + kGroup * kHeadDim * 2 + 2 * kHeadDim * 4;
+    kAttnWarps * kGroup * kPartialStride * 4 + kGroup * kHeadDim * 2 + 2 * kHeadDim * 4;
 
-__host__ __device__ inline int smem_bytes_for(int num_slots, int B, int kmax) {
-  int x = B * kmax * 2;
-  x = (x + 127) & ~127;
-  return num_slots * kSlotBytes + x + kAttnScratchBytes + 2 * num_slots * 8 +
-         (int)sizeof(SmemState) + 128;
+__host__ __device__ inline int align128(int x) { return (x + 127) & ~127; }
+
+__host__ __device__ inline int smem_bytes_for(int num_slots, int B, int kmax, int part_cap, int H) {
+  return num_slots * kSlotBytes + align128(B * kmax * 2) + align128(part_cap * 4) +
+         align128(B * H * 2) + align128(B * 2 * kHeadDim * 2) + kAttnScratchBytes +
+         2 * num_slots * 8 + (int)sizeof(SmemState) + 128;
+}
+
+// Pieces per row of K columns: the fewest equal segments of at most
+// kSegCols columns, each a multiple of 256 (32 lanes x 8 bf16).
+__host__ __device__ inline int pieces_per_row(int K) {
+  for (int n = (K + kSegCols - 1) / kSegCols; n <= K / 256; ++n)
+    if (K % n == 0 && (K / n) % 256 == 0) return n;
+  return K / 256;
 }
 
 // ---------------------------------------------------------------- errors
@@ -247,50 +273,98 @@ __device__ __forceinline__ AttnItem attn_item(const Params& p, const SmemState& 
   return a;
 }
 
+// Walk the CTA's streaming schedule for one step, in the order the consumers
+// use it: per layer the QKV rows, the KV chunks of its attention items, the
+// o_proj rows, the gate/up row pairs, the down rows; then the lm_head rows.
+// `ops` is the producer (bulk copies into the ring) or the prefetch lane.
+template <int B, class Ops>
+__device__ void walk_schedule(const Params& p, const SmemState& st, Ops& ops) {
+  Sched sch;
+  const int NQKV = p.NQ + 2 * p.NKV;
+  const int H = p.H, I = p.I, QD = p.NQ * kHeadDim;
+  const int T = B * p.NKV * st.n_split;
+  for (int l = 0; l < p.L && ops.ok; ++l) {
+    ops.mark(l * 5 + 0, true);
+    ops.units(p.w_qkv + (size_t)l * NQKV * 32 * 2 * H, 4 * H, sch.next(NQKV * 32));
+    ops.mark(l * 5 + 0, false);
+    ops.mark(l * 5 + 1, true);
+    for (int it = blockIdx.x; it < T && ops.ok; it += gridDim.x) {
+      const AttnItem a = attn_item(p, st, it);
+      for (int c0 = a.p0; c0 < a.p1 && ops.ok; c0 += kAttnChunk) {
+        ops.kv_chunk(l, a.b, a.g, c0, min(kAttnChunk, a.p1 - c0));
+      }
+    }
+    ops.mark(l * 5 + 1, false);
+    ops.mark(l * 5 + 2, true);
+    ops.units(p.w_o + (size_t)l * H * QD, 2 * QD, sch.next(H));
+    ops.mark(l * 5 + 2, false);
+    ops.mark(l * 5 + 3, true);
+    ops.units(p.w_gu + (size_t)l * I * 2 * H, 4 * H, sch.next(I));
+    ops.mark(l * 5 + 3, false);
+    ops.mark(l * 5 + 4, true);
+    ops.units(p.w_down + (size_t)l * H * I, 2 * I, sch.next(H));
+    ops.mark(l * 5 + 4, false);
+  }
+  if (p.mode == 0 && ops.ok) {
+    ops.mark(p.L * 5, true);
+    ops.units(p.embed, 2 * H, sch.next(p.V));
+    ops.mark(p.L * 5, false);
+  }
+}
+
 // ---------------------------------------------------------------- ring
 
 struct Ring {
-  uint8_t* slots;
+  uint8_t* slots;    // generic address of slot 0
+  uint32_t slots_s;  // shared-window address of slot 0
   uint64_t* full;
   uint64_t* empty;
   int S;
-  uint32_t n = 0;  // fills seen so far (same count on both sides)
+  uint32_t n = 0;  // fills seen so far (the same count on every side)
   unsigned long long stall_ns = 0;  // time spent waiting (traced runs only)
 };
 
-// Consumer warp: wait for fill n; nullptr on abort/timeout. Every lane waits
-// on the mbarrier itself; lane 0 alone decides to give up and the decision is
-// broadcast, so the result is uniform across the warp.
-__device__ __noinline__ const uint8_t* ring_wait(const Params& p, Ring& r, int where) {
-  const int slot = r.n % r.S;
-  const uint32_t parity = (r.n / r.S) & 1;
-  uint64_t* bar = &r.full[slot];
-  bool done = mbar_try_wait(bar, parity);
-  uint64_t t0 = 0;
-  const uint64_t ts = (p.trace && !__all_sync(0xffffffffu, done)) ? global_ns() : 0;
-  for (uint32_t it = 0; !__all_sync(0xffffffffu, done); ++it) {
+// Slow path of a consumer warp's wait for a fill: every lane polls the
+// mbarrier; lane 0 alone decides to give up (abort or timeout) and the
+// decision is broadcast, so the result is uniform across the warp.
+__device__ __noinline__ bool ring_wait_slow(const Params& p, uint64_t* bar, uint32_t parity,
+                                            int where) {
+  const uint64_t t0 = global_ns();
+  bool done = false;
+  for (uint32_t it = 0;; ++it) {
     if (!done) done = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
     int give_up = 0;
     if ((it & 7) == 7 && (threadIdx.x & 31) == 0) {
-      const uint64_t now = global_ns();
-      if (t0 == 0) t0 = now;
       if (aborted(p)) {
         give_up = 1;
-      } else if (now - t0 > p.timeout_ns) {
+      } else if (global_ns() - t0 > p.timeout_ns) {
         raise_error(p, kErrRingTimeout, where);
         give_up = 1;
       }
     }
-    if (__shfl_sync(0xffffffffu, give_up, 0)) return nullptr;
+    if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
   }
-  if (ts) r.stall_ns += global_ns() - ts;
-  return r.slots + (size_t)slot * kSlotBytes;
 }
 
-__device__ __forceinline__ void ring_release(Ring& r) {
+// Consumer warp: wait until fill `f` has landed. false on abort/timeout.
+__device__ __forceinline__ bool ring_wait(const Params& p, Ring& r, uint32_t f, int where) {
+  uint64_t* bar = &r.full[f % r.S];
+  const uint32_t parity = (f / r.S) & 1;
+  // try_wait may itself suspend the thread for a while, so a traced run
+  // times the whole wait.
+  const uint64_t ts = p.trace ? global_ns() : 0;
+  bool ok = __all_sync(0xffffffffu, mbar_try_wait(bar, parity));
+  if (!ok) ok = ring_wait_slow(p, bar, parity, where);
+  if (ts) r.stall_ns += global_ns() - ts;
+  return ok;
+}
+
+// Consumer warp: done with fill `f`; `count` arrivals on its empty barrier
+// (the warps that read a fill contribute kConsumerWarps arrivals in total).
+__device__ __forceinline__ void ring_release(Ring& r, uint32_t f, uint32_t count) {
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(&r.empty[r.n % r.S]);
-  r.n++;
+  if ((threadIdx.x & 31) == 0) mbar_arrive_cnt(&r.empty[f % r.S], count);
 }
 
 // ---------------------------------------------------------------- producer
@@ -298,6 +372,7 @@ __device__ __forceinline__ void ring_release(Ring& r) {
 struct Producer {
   const Params& p;
   Ring& r;
+  SmemState& st;
   uint64_t pol;
   bool ok = true;
 
@@ -318,7 +393,20 @@ struct Producer {
     return r.slots + (size_t)slot * kSlotBytes;
   }
   __device__ uint64_t* bar() { return &r.full[r.n % r.S]; }
-  __device__ void end() { r.n++; }
+  __device__ void end() {
+    r.n++;
+    *reinterpret_cast<volatile uint32_t*>(&st.prod_fills) = r.n;
+  }
+
+  __device__ void mark(int ph, bool start) {
+    if (!p.trace) return;
+    if (start) {
+      trace_put(p, ph, kTrProdStart, global_ns());
+    } else {
+      trace_put(p, ph, kTrProdEnd, global_ns());
+      trace_put(p, ph, kTrProdStall, r.stall_ns);
+    }
+  }
 
   // Stream units [u0, u1) of `unit_bytes` each from `base`, packed per slot.
   __device__ void units(const bf16* base, int unit_bytes, Split sp) {
@@ -374,51 +462,82 @@ struct Producer {
   }
 };
 
-template <int B>
-__device__ void run_producer(const Params& p, const SmemState& st, Ring& ring) {
-  Producer pr{p, ring, policy_evict_first()};
-  Sched sch;
-  const int NQKV = p.NQ + 2 * p.NKV;
-  const int H = p.H, I = p.I, QD = p.NQ * kHeadDim;
-  const int T = B * p.NKV * st.n_split;
-  auto mark = [&](int ph, bool start) {
-    if (!p.trace) return;
-    if (start) {
-      trace_put(p, ph, kTrProdStart, global_ns());
-    } else {
-      trace_put(p, ph, kTrProdEnd, global_ns());
-      trace_put(p, ph, kTrProdStall, ring.stall_ns);
-    }
-  };
-  for (int l = 0; l < p.L && pr.ok; ++l) {
-    mark(l * 5 + 0, true);
-    pr.units(p.w_qkv + (size_t)l * NQKV * 32 * 2 * H, 4 * H, sch.next(NQKV * 32));
-    mark(l * 5 + 0, false);
-    mark(l * 5 + 1, true);
-    for (int it = blockIdx.x; it < T && pr.ok; it += gridDim.x) {
-      const AttnItem a = attn_item(p, st, it);
-      for (int c0 = a.p0; c0 < a.p1 && pr.ok; c0 += kAttnChunk) {
-        pr.kv_chunk(l, a.b, a.g, c0, min(kAttnChunk, a.p1 - c0));
+// The prefetch lane: the producer's schedule as L2 prefetches, at most
+// `prefetch_slots` fills ahead of it and paced to a fixed byte rate, so HBM
+// keeps streaming while the consumers sit in barriers or attention, without
+// flooding the memory system with requests (which would delay the
+// latency-bound barrier and activation traffic). Nothing waits for a
+// prefetch, so on any failure the lane just stops.
+struct Prefetcher {
+  const Params& p;
+  const SmemState& st;
+  uint32_t n = 0;
+  bool ok = true;
+  uint64_t t_next = 0;  // earliest globaltimer ns for the next prefetch
+
+  // Fill n may be prefetched once the producer has issued fill n - lead and
+  // the pacing clock allows it.
+  __device__ bool gate() {
+    const uint32_t lead = (uint32_t)p.prefetch_slots;
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+      const uint32_t prod = *reinterpret_cast<const volatile uint32_t*>(&st.prod_fills);
+      if (n < prod + lead && (t_next == 0 || global_ns() >= t_next)) return true;
+      if ((it & 15) == 15) {
+        if (aborted(p)) return false;
+        const uint64_t now = global_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > p.timeout_ns) {
+          return false;
+        }
       }
+      __nanosleep(64);
     }
-    mark(l * 5 + 1, false);
-    mark(l * 5 + 2, true);
-    pr.units(p.w_o + (size_t)l * H * QD, 2 * QD, sch.next(H));
-    mark(l * 5 + 2, false);
-    mark(l * 5 + 3, true);
-    pr.units(p.w_gu + (size_t)l * I * 2 * H, 4 * H, sch.next(I));
-    mark(l * 5 + 3, false);
-    mark(l * 5 + 4, true);
-    pr.units(p.w_down + (size_t)l * H * I, 2 * I, sch.next(H));
-    mark(l * 5 + 4, false);
   }
-  if (p.mode == 0 && pr.ok) {
-    mark(p.L * 5, true);
-    pr.units(p.embed, 2 * H, sch.next(p.V));
-    mark(p.L * 5, false);
+  __device__ void mark(int, bool) {}
+
+  __device__ void pace(uint32_t bytes) {
+    if (p.prefetch_ns_per_byte > 0.f) {
+      const uint64_t now = global_ns();
+      const uint64_t base = (t_next > now || t_next == 0) ? (t_next ? t_next : now) : now;
+      t_next = base + (uint64_t)(bytes * p.prefetch_ns_per_byte);
+    }
   }
-  if (!pr.ok) pr.drain();
-}
+
+  __device__ void units(const bf16* base, int unit_bytes, Split sp) {
+    const int ups = units_per_slot(unit_bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(base);
+    for (int u = sp.u0; u < sp.u1 && ok; u += ups) {
+      const int k = min(ups, sp.u1 - u);
+      if (!(ok = gate())) return;
+      prefetch_l2(src + (size_t)u * unit_bytes, (uint32_t)k * unit_bytes);
+      pace((uint32_t)k * unit_bytes);
+      n++;
+    }
+  }
+
+  __device__ void kv_chunk(int layer, int b, int g, int c0, int cnt) {
+    if (!(ok = gate())) return;
+    const int ps = p.page_size;
+    const size_t layer_off = (size_t)layer * p.num_pages * p.NKV * ps * kHeadDim;
+    for (int q = c0; q < c0 + cnt;) {
+      const int off = q % ps;
+      const int run = min(c0 + cnt - q, ps - off);
+      const int page = __ldg(p.block_tables + b * p.max_blocks + q / ps);
+      if (page < 0 || page >= p.num_pages) {
+        ok = false;  // the producer reports it
+        return;
+      }
+      const size_t src_off = layer_off + (((size_t)page * p.NKV + g) * ps + off) * kHeadDim;
+      prefetch_l2(p.k_pages + src_off, (uint32_t)run * kHeadDim * 2);
+      prefetch_l2(p.v_pages + src_off, (uint32_t)run * kHeadDim * 2);
+      q += run;
+    }
+    pace((uint32_t)cnt * kHeadDim * 4);
+    n++;
+  }
+};
 
 // ---------------------------------------------------------------- consumers
 
@@ -426,7 +545,7 @@ __device__ void run_producer(const Params& p, const SmemState& st, Ring& ring) {
 // HF RMSNorm: y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * gamma).
 template <int B>
 __device__ void load_rows(const bf16* const (&src)[B], int K, const bf16* gamma, float eps,
-                          bf16* xs, int kmax, SmemState& st) {
+                          bf16* xs, int kmax, SmemState& st, bf16* raw = nullptr) {
   const int tid = threadIdx.x;
   const int kv = K >> 3;
   float ss[B];
@@ -437,6 +556,7 @@ __device__ void load_rows(const bf16* const (&src)[B], int K, const bf16* gamma,
     for (int b = 0; b < B; ++b) {
       const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src[b]) + v);
       reinterpret_cast<uint4*>(xs + b * kmax)[v] = u;
+      if (raw) reinterpret_cast<uint4*>(raw + b * K)[v] = u;
       if (gamma) {
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -506,48 +626,84 @@ __device__ __forceinline__ float dot8(const uint4& w, const float (&x)[8], float
   return acc;
 }
 
-// One phase of row reductions: every streamed unit is ROWS rows of K bf16;
-// the warp (unit index mod 8) reduces it against the B activation rows in xs
-// and hands the fp32 sums (valid in every lane) to `epi(unit, acc)`.
-template <int B, int ROWS, class Epi>
-__device__ bool rows_phase(const Params& p, Ring& ring, const bf16* xs, int K, Split sp,
-                           int where, Epi&& epi) {
+// One streamed GEMV phase over units [sp.u0, sp.u1): each unit is
+// `rows_per_unit` rows of K bf16 columns, cut into pieces of K / nseg
+// columns. Work items are groups of `grp` consecutive pieces (1, or a whole
+// row when the caller needs full-row sums); item t goes to warp t mod 16.
+// The warp reduces its item against the B activation rows in shared memory
+// (kept in registers for B == 1) and calls out(t, sums, lane) with the fp32
+// sums valid in every lane.
+template <int B, class Out>
+__device__ __noinline__ bool gemv_phase(const Params& p, Ring& ring_io, uint32_t xs_s, int K,
+                                        int nseg, int rows_per_unit, int grp, Split sp, int where,
+                                        Out&& out) {
+  constexpr int NC = kConsumerWarps;
+  Ring ring = ring_io;  // registers for the loop; written back on every exit
+  struct WriteBack {
+    Ring& dst;
+    const Ring& src;
+    __device__ ~WriteBack() {
+      dst.n = src.n;
+      dst.stall_ns = src.stall_ns;
+    }
+  } wb{ring_io, ring};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int unit_bytes = ROWS * K * 2;
+  const int seg = K / nseg;
+  const int CH = seg >> 8;
+  const int piece_bytes = seg * 2;
+  const int unit_bytes = rows_per_unit * K * 2;
   const int ups = units_per_slot(unit_bytes);
-  const int kv = K >> 3;
+  const int ipu = rows_per_unit * nseg / grp;  // items per unit
+  uint4 xr[8];
+  int cached = -1;
   for (int s0 = sp.u0; s0 < sp.u1; s0 += ups) {
     const int n = min(ups, sp.u1 - s0);
-    const uint8_t* slot = ring_wait(p, ring, where);
-    if (!slot) return false;
-    for (int i = 0; i < n; ++i) {
-      if (((s0 - sp.u0 + i) & (kConsumerWarps - 1)) != warp) continue;
-      const uint4* w = reinterpret_cast<const uint4*>(slot + i * unit_bytes);
-      float acc[ROWS][B];
+    const int P = n * ipu;                 // items in this fill
+    const int t0 = (s0 - sp.u0) * ipu;     // phase-local index of its first item
+    const uint32_t f = ring.n++;
+    const int lead = t0 % NC;
+    const int first = t0 + (warp - lead + NC) % NC;
+    if (first >= t0 + P) continue;
+    if (!ring_wait(p, ring, f, where)) return false;
+    const uint32_t sbase = ring.slots_s + (f % ring.S) * kSlotBytes + lane * 16;
+    for (int t = first; t < t0 + P; t += NC) {
+      float acc[B][4];
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r)
+      for (int b = 0; b < B; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.f;
+      for (int k = 0; k < grp; ++k) {
+        const int q = t * grp + k;  // phase-local piece index
+        const int j = q % nseg;     // its column segment
+        if (B == 1 && j != cached) {
+          const uint32_t xa = xs_s + (uint32_t)(j * seg + lane * 8) * 2;
 #pragma unroll
-        for (int b = 0; b < B; ++b) acc[r][b] = 0.f;
-#pragma unroll 4
-      for (int v = lane; v < kv; v += 32) {
-        uint4 wr[ROWS];
+          for (int c = 0; c < 8; ++c)
+            if (c < CH) xr[c] = lds128(xa + c * 512);
+          cached = j;
+        }
+        const uint32_t wa = sbase + (uint32_t)(q - t0 * grp) * piece_bytes;
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) wr[r] = w[r * kv + v];
+        for (int c = 0; c < 8; ++c) {
+          if (c < CH) {
+            const uint4 w = lds128(wa + c * 512);
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-          float xf[8];
-          unpack8(reinterpret_cast<const uint4*>(xs + b * p.kmax)[v], xf);
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) acc[r][b] = dot8(wr[r], xf, acc[r][b]);
+            for (int b = 0; b < B; ++b) {
+              const uint4 x =
+                  (B == 1) ? xr[c]
+                           : lds128(xs_s + (uint32_t)(b * p.kmax + j * seg + c * 256 + lane * 8) * 2);
+              fma2_bf16(w.x, x.x, acc[b][0], acc[b][1]);
+              fma2_bf16(w.y, x.y, acc[b][2], acc[b][3]);
+              fma2_bf16(w.z, x.z, acc[b][0], acc[b][1]);
+              fma2_bf16(w.w, x.w, acc[b][2], acc[b][3]);
+            }
+          }
         }
       }
+      float v[B];
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r)
-#pragma unroll
-        for (int b = 0; b < B; ++b) acc[r][b] = warp_sum(acc[r][b]);
-      epi(s0 + i, acc, lane);
+      for (int b = 0; b < B; ++b) v[b] = warp_sum((acc[b][0] + acc[b][1]) + (acc[b][2] + acc[b][3]));
+      out(t, v, lane);
     }
-    ring_release(ring);
+    ring_release(ring, f, (P < NC && warp == lead) ? (uint32_t)(NC - P + 1) : 1u);
   }
   return true;
 }
@@ -557,10 +713,9 @@ __device__ bool rows_phase(const Params& p, Ring& ring, const bf16* xs, int K, S
 // consumer threads see the same answer).
 __device__ __forceinline__ bool grid_arrive(const Params& p, bool ok, bool skip) {
   if (consumer_any(!ok)) return false;
-  if (threadIdx.x == 0 && !skip) {
-    __threadfence();
-    red_release_add_u32(p.counters + kCntBarrier, 1u);
-  }
+  // The release add is cumulative: the CTA's writes, ordered before it by
+  // the named barrier above, are visible to any CTA that acquires the count.
+  if (threadIdx.x == 0 && !skip) red_release_add_u32(p.counters + kCntBarrier, 1u);
   return true;
 }
 
@@ -572,10 +727,54 @@ __device__ __forceinline__ bool grid_wait(const Params& p, uint32_t* counter, ui
   return !consumer_any(!ok);
 }
 
+static_assert(kConsumerThreads >= kGroup * kHeadDim + kGroup * kMaxSplit,
+              "merge_group needs a thread per (head, dim) plus one per (head, split)");
+
+// The last split to finish a (seq b, kv head g) merges every split's
+// (m, l, o) — split 0 already holds the new token's own K/V — and writes the
+// group's bf16 head outputs. All consumer threads call it. The per-split
+// loads are issued before any is used, so the merge costs one L2 round trip.
+__device__ __noinline__ void merge_group(const Params& p, int b, int g, int ns, float* ml) {
+  const int tid = threadIdx.x;
+  const float* base = p.partials + ((size_t)b * p.NKV + g) * kMaxSplit * kGroup * kPartialStride;
+  const bool worker = tid < kGroup * kHeadDim;
+  const int hh = (tid >> 6) & (kGroup - 1), d = tid & 63;
+  float os[kMaxSplit];
+  if (worker) {
+#pragma unroll
+    for (int s = 0; s < kMaxSplit; ++s)
+      if (s < ns) os[s] = __ldcg(base + (size_t)(s * kGroup + hh) * kPartialStride + d);
+  } else if (tid < kGroup * kHeadDim + kGroup * ns) {
+    const int i = tid - kGroup * kHeadDim, h2 = i / ns, s = i % ns;
+    const float* ps = base + (size_t)(s * kGroup + h2) * kPartialStride;
+    ml[(h2 * kMaxSplit + s) * 2] = __ldcg(ps + kHeadDim);
+    ml[(h2 * kMaxSplit + s) * 2 + 1] = __ldcg(ps + kHeadDim + 1);
+  }
+  consumer_sync();
+  if (worker) {
+    const float* mh = ml + hh * kMaxSplit * 2;
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kMaxSplit; ++s)
+      if (s < ns) M = fmaxf(M, mh[2 * s]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxSplit; ++s) {
+      if (s < ns && mh[2 * s] > -INFINITY) {
+        const float f = __expf(mh[2 * s] - M);
+        L += f * mh[2 * s + 1];
+        O += f * os[s];
+      }
+    }
+    p.attn[(size_t)b * p.NQ * kHeadDim + (g * kGroup + hh) * kHeadDim + d] = f2bf(O / L);
+  }
+}
+
 template <int B>
 __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int layer,
                                 float* comb, bf16* qs, float* kvn) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool attn_warp = warp < kAttnWarps;
   const int NQKV = p.NQ + 2 * p.NKV;
   const int T = B * p.NKV * st.n_split;
   const float scale = 0.125f;  // head_dim ** -0.5
@@ -583,11 +782,23 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
   for (int it = blockIdx.x; it < T; it += gridDim.x) {
     const AttnItem a = attn_item(p, st, it);
     consumer_sync();
+    // q of the group's heads, and the new token's own K and V row (used by
+    // the last split's merge), in one round trip.
     if (tid < kGroup * kHeadDim / 8) {
       reinterpret_cast<uint4*>(qs)[tid] =
           __ldcg(reinterpret_cast<const uint4*>(p.qkv + ((size_t)a.b * NQKV + a.g * kGroup) * kHeadDim) + tid);
+    } else if (tid < kGroup * kHeadDim / 8 + 16) {
+      const int r = tid - kGroup * kHeadDim / 8;  // 0..7 K, 8..15 V
+      const int head = (r < 8) ? p.NQ + a.g : p.NQ + p.NKV + a.g;
+      const uint4 u =
+          __ldcg(reinterpret_cast<const uint4*>(p.qkv + ((size_t)a.b * NQKV + head) * kHeadDim) + (r & 7));
+      float f[8];
+      unpack8(u, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kvn[(r >> 3) * kHeadDim + (r & 7) * 8 + e] = f[e];
     }
     consumer_sync();
+    if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnQ, global_ns());
     float m = -INFINITY, l = 0.f, o[8];
     bool fail = false;
 #pragma unroll
@@ -595,11 +806,13 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
     const uint4* q4 = reinterpret_cast<const uint4*>(qs + h * kHeadDim);
     for (int c0 = a.p0; c0 < a.p1; c0 += kAttnChunk) {
       const int n = min(kAttnChunk, a.p1 - c0);
-      const uint8_t* slot = ring_wait(p, ring, 200 + layer);
-      if (!slot) {
+      const uint32_t f = ring.n++;
+      if (!attn_warp || fail) continue;
+      if (!ring_wait(p, ring, f, 200 + layer)) {
         fail = true;
-        break;
+        continue;
       }
+      const uint8_t* slot = ring.slots + (size_t)(f % ring.S) * kSlotBytes;
       const int pc = warp * 8 + j;
       const bool valid = pc < n;
       float sc = -INFINITY;
@@ -646,27 +859,51 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
         }
         m = m_new;
       }
-      ring_release(ring);
+      ring_release(ring, f, warp == 0 ? (uint32_t)(kConsumerWarps - kAttnWarps + 1) : 1u);
     }
-    // Merge the 8 warps' (m, l, o) for each q head of the group.
-    float* cw = comb + (warp * kGroup + h) * kPartialStride;
+    // Split 0 also takes the new token's own K/V (the "active slot"), on
+    // warp 0: lane (h, j) adds dims [8j, 8j + 8) of q_h . k_new, reduced
+    // over the head's eight lanes.
+    if (a.s == 0 && warp == 0) {
+      float qf[8];
+      unpack8(q4[j], qf);
+      float sa = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) cw[j * 8 + e] = o[e];
-    if (j == 0) {
-      cw[kHeadDim] = m;
-      cw[kHeadDim + 1] = l;
+      for (int e = 0; e < 8; ++e) sa = fmaf(qf[e], kvn[j * 8 + e], sa);
+      sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+      sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+      sa += __shfl_xor_sync(0xffffffffu, sa, 4);
+      sa *= scale;
+      const float m_new = fmaxf(m, sa);
+      const float alpha = (m == -INFINITY) ? 0.f : __expf(m - m_new);
+      const float pe = __expf(sa - m_new);
+      l = l * alpha + pe;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = o[e] * alpha + pe * kvn[kHeadDim + j * 8 + e];
+      m = m_new;
+    }
+    if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnChunks, global_ns());
+    // Merge the attention warps' (m, l, o) for each q head of the group.
+    if (attn_warp) {
+      float* cw = comb + (warp * kGroup + h) * kPartialStride;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cw[j * 8 + e] = o[e];
+      if (j == 0) {
+        cw[kHeadDim] = m;
+        cw[kHeadDim + 1] = l;
+      }
     }
     if (consumer_any(fail)) return false;
-    {
+    if (tid < kGroup * kHeadDim) {
       const int hh = tid >> 6, d = tid & 63;
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w)
+      for (int w = 0; w < kAttnWarps; ++w)
         M = fmaxf(M, comb[(w * kGroup + hh) * kPartialStride + kHeadDim]);
       float L = 0.f, O = 0.f;
       if (M > -INFINITY) {
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
+        for (int w = 0; w < kAttnWarps; ++w) {
           const float* cwp = comb + (w * kGroup + hh) * kPartialStride;
           const float mw = cwp[kHeadDim];
           if (mw > -INFINITY) {
@@ -685,53 +922,22 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
       }
     }
     consumer_sync();
+    // Count the split; the last one of its (seq, kv head) merges them all.
     if (tid == 0) {
-      __threadfence();
       uint32_t* arr = p.counters + kCntArrive + a.b * p.NKV + a.g;
-      const uint32_t old = atomicAdd(arr, 1u);
+      const uint32_t old = atom_add_acq_rel_u32(arr, 1u);
       const int last = (old == (uint32_t)(st.n_split - 1)) ? 1 : 0;
-      if (last) {
-        atomicExch(arr, 0u);
-        __threadfence();
-      }
+      if (last) atomicExch(arr, 0u);
       st.flag = last;
+      if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
     }
     consumer_sync();
     if (st.flag) {
-      // Last split of this (seq, kv head): merge all splits plus the new
-      // token's own K/V (the "active slot"), then publish the heads.
-      const bf16* kn = p.qkv + ((size_t)a.b * NQKV + p.NQ + a.g) * kHeadDim;
-      const bf16* vn = p.qkv + ((size_t)a.b * NQKV + p.NQ + p.NKV + a.g) * kHeadDim;
-      if (tid < kHeadDim) {
-        kvn[tid] = bf2f(__ldcg(kn + tid));
-        kvn[kHeadDim + tid] = bf2f(__ldcg(vn + tid));
-      }
-      consumer_sync();
-      const int hh = tid >> 6, d = tid & 63;
-      float sa = 0.f;
-      for (int e = 0; e < kHeadDim; ++e) sa = fmaf(bf2f(qs[hh * kHeadDim + e]), kvn[e], sa);
-      sa *= scale;
-      float M = sa;
-      const float* base =
-          p.partials + (((size_t)a.b * p.NKV + a.g) * kMaxSplit * kGroup + hh) * kPartialStride;
-      for (int s = 0; s < st.n_split; ++s)
-        M = fmaxf(M, __ldcg(base + (size_t)s * kGroup * kPartialStride + kHeadDim));
-      float L = __expf(sa - M);
-      float O = L * kvn[kHeadDim + d];
-      for (int s = 0; s < st.n_split; ++s) {
-        const float* ps = base + (size_t)s * kGroup * kPartialStride;
-        const float ms = __ldcg(ps + kHeadDim);
-        if (ms > -INFINITY) {
-          const float f = __expf(ms - M);
-          L += f * __ldcg(ps + kHeadDim + 1);
-          O += f * __ldcg(ps + d);
-        }
-      }
-      p.attn[(size_t)a.b * p.NQ * kHeadDim + (a.g * kGroup + hh) * kHeadDim + d] = f2bf(O / L);
+      merge_group(p, a.b, a.g, st.n_split, comb);
       consumer_sync();
       if (tid == 0) {
-        __threadfence();
         red_release_add_u32(p.counters + kCntHeadsDone, 1u);
+        if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnMerged, global_ns());
       }
     }
   }
@@ -739,15 +945,21 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
 }
 
 template <int B>
-__device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* xs,
-                              float* comb, bf16* qs, float* kvn) {
+__device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* xs, float* part,
+                              float* comb, bf16* qs, float* kvn, bf16* raw, bf16* rope) {
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
+  // This step's RoPE rows (cos, sin per sequence), used by every layer.
+  if (tid < B * 2 * kHeadDim / 8) {
+    const int b = tid / (2 * kHeadDim / 8), r = tid % (2 * kHeadDim / 8);
+    const bf16* tab = (r < kHeadDim / 8) ? p.rope_cos : p.rope_sin;
+    reinterpret_cast<uint4*>(rope + b * 2 * kHeadDim)[r] =
+        __ldg(reinterpret_cast<const uint4*>(tab + (size_t)st.pos[b] * kHeadDim) + (r % (kHeadDim / 8)));
+  }
   const int H = p.H, I = p.I, QD = p.NQ * kHeadDim, NQKV = p.NQ + 2 * p.NKV;
+  const uint32_t xs_s = smem_addr(xs);
   Sched sch;
   uint32_t barriers = 0;  // grid barriers passed so far
   const int G = gridDim.x;
-  (void)warp;
   auto mark = [&](int ph, int kind) {
     if (p.trace && threadIdx.x == 0) trace_put(p, ph, kind, global_ns());
   };
@@ -756,6 +968,19 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       trace_put(p, ph, kTrDone, global_ns());
       trace_put(p, ph, kTrConsStall, ring.stall_ns);
     }
+  };
+  // Phase-local partial sums: part[piece * B + b].
+  auto to_part = [&](int q, float (&v)[B], int lane) {
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < B; ++b) part[q * B + b] = v[b];
+    }
+  };
+  // Sum of a row's nseg pieces (fixed order).
+  auto row_sum = [&](int q0, int nseg, int b) {
+    float s = part[q0 * B + b];
+    for (int k = 1; k < nseg; ++k) s += part[(q0 + k) * B + b];
+    return s;
   };
 
   for (int l = 0; l < p.L; ++l) {
@@ -772,21 +997,24 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         src[b] = (l > 0) ? p.h + (size_t)b * H
                  : (p.mode == 0 ? p.embed + (size_t)st.tok[b] * H : p.hidden_in + (size_t)b * H);
       }
-      load_rows<B>(src, H, p.norm_attn + (size_t)l * H, p.eps, xs, p.kmax, st);
+      load_rows<B>(src, H, p.norm_attn + (size_t)l * H, p.eps, xs, p.kmax, st, raw);
     }
     mark(l * 5 + 0, kTrRowsLoaded);
     const Split sq = sch.next(NQKV * 32);
-    const size_t kv_layer = (size_t)l * p.num_pages * p.NKV * p.page_size * kHeadDim;
-    bool ok = rows_phase<B, 2>(p, ring, xs, H, sq, 2000 + l, [&](int u, float (&acc)[2][B], int lane) {
-      const int hh = u >> 5, d = u & 31;
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        if (lane != b) continue;
-        float x0 = rbf(acc[0][b]), x1 = rbf(acc[1][b]);
+    bool ok = gemv_phase<B>(p, ring, xs_s, H, p.nseg_h, 2, 1, sq, 2000 + l, to_part);
+    if (consumer_any(!ok)) return;
+    {
+      const size_t kv_layer = (size_t)l * p.num_pages * p.NKV * p.page_size * kHeadDim;
+      const int nu = sq.u1 - sq.u0, ns = p.nseg_h;
+      for (int i = tid; i < nu * B; i += kConsumerThreads) {
+        const int ul = i / B, b = i % B, u = sq.u0 + ul;
+        const int hh = u >> 5, d = u & 31;
+        float x0 = rbf(row_sum(ul * 2 * ns, ns, b));
+        float x1 = rbf(row_sum(ul * 2 * ns + ns, ns, b));
         const int pos = st.pos[b];
         if (hh < p.NQ + p.NKV) {
-          const bf16* cr = p.rope_cos + (size_t)pos * kHeadDim;
-          const bf16* sr = p.rope_sin + (size_t)pos * kHeadDim;
+          const bf16* cr = rope + b * 2 * kHeadDim;
+          const bf16* sr = cr + kHeadDim;
           const float c0 = bf2f(cr[d]), c1 = bf2f(cr[d + 32]);
           const float s0 = bf2f(sr[d]), s1 = bf2f(sr[d + 32]);
           const float y0 = rbf(rbf(x0 * c0) + rbf(-x1 * s0));
@@ -811,7 +1039,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
           }
         }
       }
-    });
+    }
     mark_done(l * 5 + 0);
     if (!grid_arrive(p, ok, l == 0 && (int)blockIdx.x == p.debug_skip_cta)) return;
     ++barriers;
@@ -835,16 +1063,18 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       load_rows<B>(src, QD, nullptr, 0.f, xs, p.kmax, st);
     }
     mark(l * 5 + 2, kTrRowsLoaded);
-    ok = rows_phase<B, 1>(p, ring, xs, QD, sch.next(H), 5000 + l, [&](int u, float (&acc)[1][B], int lane) {
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        if (lane != b) continue;
-        const bf16* res = (l > 0) ? p.h + (size_t)b * H
-                          : (p.mode == 0 ? p.embed + (size_t)st.tok[b] * H : p.hidden_in + (size_t)b * H);
-        const float r = bf2f(__ldcg(res + u));
-        p.h[(size_t)b * H + u] = f2bf(r + rbf(acc[0][b]));
+    {
+      const Split so = sch.next(H);
+      ok = gemv_phase<B>(p, ring, xs_s, QD, p.nseg_qd, 1, 1, so, 5000 + l, to_part);
+      if (consumer_any(!ok)) return;
+      const int nu = so.u1 - so.u0, ns = p.nseg_qd;
+      for (int i = tid; i < nu * B; i += kConsumerThreads) {
+        const int ul = i / B, b = i % B, u = so.u0 + ul;
+        // residual: the layer input, kept raw by the QKV phase's row load
+        const float r = bf2f(raw[b * H + u]);
+        p.h[(size_t)b * H + u] = f2bf(r + rbf(row_sum(ul * ns, ns, b)));
       }
-    });
+    }
     mark_done(l * 5 + 2);
     if (!grid_arrive(p, ok, false)) return;
     ++barriers;
@@ -857,19 +1087,22 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       const bf16* src[B];
 #pragma unroll
       for (int b = 0; b < B; ++b) src[b] = p.h + (size_t)b * H;
-      load_rows<B>(src, H, p.norm_mlp + (size_t)l * H, p.eps, xs, p.kmax, st);
+      load_rows<B>(src, H, p.norm_mlp + (size_t)l * H, p.eps, xs, p.kmax, st, raw);
     }
     mark(l * 5 + 3, kTrRowsLoaded);
-    ok = rows_phase<B, 2>(p, ring, xs, H, sch.next(I), 7000 + l, [&](int u, float (&acc)[2][B], int lane) {
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        if (lane != b) continue;
-        const float g = rbf(acc[0][b]);
-        const float up = rbf(acc[1][b]);
+    {
+      const Split sg = sch.next(I);
+      ok = gemv_phase<B>(p, ring, xs_s, H, p.nseg_h, 2, 1, sg, 7000 + l, to_part);
+      if (consumer_any(!ok)) return;
+      const int nu = sg.u1 - sg.u0, ns = p.nseg_h;
+      for (int i = tid; i < nu * B; i += kConsumerThreads) {
+        const int ul = i / B, b = i % B, u = sg.u0 + ul;
+        const float g = rbf(row_sum(ul * 2 * ns, ns, b));
+        const float up = rbf(row_sum(ul * 2 * ns + ns, ns, b));
         const float s = rbf(__fdiv_rn(g, 1.0f + expf(-g)));
         p.act[(size_t)b * I + u] = f2bf(s * up);
       }
-    });
+    }
     mark_done(l * 5 + 3);
     if (!grid_arrive(p, ok, false)) return;
     ++barriers;
@@ -886,19 +1119,23 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
     }
     mark(l * 5 + 4, kTrRowsLoaded);
     const bool last_layer = (l == p.L - 1);
-    ok = rows_phase<B, 1>(p, ring, xs, I, sch.next(H), 9000 + l, [&](int u, float (&acc)[1][B], int lane) {
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        if (lane != b) continue;
-        const float r = bf2f(__ldcg(p.h + (size_t)b * H + u));
-        const bf16 y = f2bf(r + rbf(acc[0][b]));
+    {
+      const Split sd = sch.next(H);
+      ok = gemv_phase<B>(p, ring, xs_s, I, p.nseg_i, 1, 1, sd, 9000 + l, to_part);
+      if (consumer_any(!ok)) return;
+      const int nu = sd.u1 - sd.u0, ns = p.nseg_i;
+      for (int i = tid; i < nu * B; i += kConsumerThreads) {
+        const int ul = i / B, b = i % B, u = sd.u0 + ul;
+        // residual: h after o_proj, kept raw by the GU phase's row load
+        const float r = bf2f(raw[b * H + u]);
+        const bf16 y = f2bf(r + rbf(row_sum(ul * ns, ns, b)));
         p.h[(size_t)b * H + u] = y;
         if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = y;
       }
-    });
+    }
     mark_done(l * 5 + 4);
     if (last_layer && p.mode == 1) {
-      if (consumer_any(!ok)) return;
+      consumer_sync();
     } else {
       if (!grid_arrive(p, ok, false)) return;
       ++barriers;
@@ -924,13 +1161,17 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       best_v[b] = -INFINITY;
       best_i[b] = 0x7fffffff;
     }
-    const bool ok = rows_phase<B, 1>(p, ring, xs, H, sch.next(p.V), 11000, [&](int u, float (&acc)[1][B], int lane) {
+    const Split sl = sch.next(p.V);
+    // One item per lm_head row (all its pieces), so the warp has the logit.
+    const bool ok = gemv_phase<B>(p, ring, xs_s, H, p.nseg_h, 1, p.nseg_h, sl, 11000,
+                                  [&](int t, float (&v)[B], int lane) {
+      if (lane != 0) return;
+      const int u = sl.u0 + t;
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        const float v = acc[0][b];
-        if (p.logits && lane == b) p.logits[(size_t)b * p.V + u] = v;
-        if (v > best_v[b] || (v == best_v[b] && u < best_i[b])) {
-          best_v[b] = v;
+        if (p.logits) p.logits[(size_t)b * p.V + u] = v[b];
+        if (v[b] > best_v[b] || (v[b] == best_v[b] && u < best_i[b])) {
+          best_v[b] = v[b];
           best_i[b] = u;
         }
       }
@@ -968,10 +1209,8 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
   // --------------------------------------------------------------- finish
   consumer_sync();
   if (tid == 0) {
-    __threadfence();
-    const uint32_t t = atomicAdd(p.counters + kCntDone, 1u);
+    const uint32_t t = atom_add_acq_rel_u32(p.counters + kCntDone, 1u);
     if (t == (uint32_t)G - 1) {
-      __threadfence();
       if (p.mode == 0) {
         for (int b = 0; b < B; ++b) {
           const unsigned long long key = atomicExch(p.keys + b, 0ull);
@@ -995,16 +1234,25 @@ template <int B>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int S = p.num_slots;
-  uint8_t* ring_mem = smem;
-  bf16* xs = reinterpret_cast<bf16*>(smem + (size_t)S * kSlotBytes);
-  int xbytes = (B * p.kmax * 2 + 127) & ~127;
-  float* comb = reinterpret_cast<float*>(smem + (size_t)S * kSlotBytes + xbytes);
-  bf16* qs = reinterpret_cast<bf16*>(comb + kConsumerWarps * kGroup * kPartialStride);
+  uint8_t* cur = smem;
+  uint8_t* ring_mem = cur;
+  cur += (size_t)S * kSlotBytes;
+  bf16* xs = reinterpret_cast<bf16*>(cur);
+  cur += align128(B * p.kmax * 2);
+  float* part = reinterpret_cast<float*>(cur);
+  cur += align128(p.part_cap * 4);
+  bf16* raw = reinterpret_cast<bf16*>(cur);
+  cur += align128(B * p.H * 2);
+  bf16* rope = reinterpret_cast<bf16*>(cur);
+  cur += align128(B * 2 * kHeadDim * 2);
+  float* comb = reinterpret_cast<float*>(cur);
+  bf16* qs = reinterpret_cast<bf16*>(comb + kAttnWarps * kGroup * kPartialStride);
   float* kvn = reinterpret_cast<float*>(qs + kGroup * kHeadDim);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * kSlotBytes + xbytes + kAttnScratchBytes);
+  cur += kAttnScratchBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cur);
   SmemState* st = reinterpret_cast<SmemState*>(bars + 2 * S);
 
-  Ring ring{ring_mem, bars, bars + S, S};
+  Ring ring{ring_mem, smem_addr(ring_mem), bars, bars + S, S};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -1029,21 +1277,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       }
       pmax = max(pmax, pos);
     }
-    // Split-K pieces per (seq, kv head): enough to spread the items over the
-    // grid, but no piece shorter than one 64-position chunk.
+    // Split-K pieces per (seq, kv head): at most one item per CTA, and no
+    // piece shorter than kSplitMinPositions (fewer partials to merge).
     int ns = min(kMaxSplit, max(1, (int)gridDim.x / (B * p.NKV)));
-    ns = max(1, min(ns, (pmax + kAttnChunk - 1) / kAttnChunk));
+    ns = max(1, min(ns, (pmax + kSplitMinPositions - 1) / kSplitMinPositions));
     st->n_split = ns;
     st->flag = bad ? 1 : 0;
+    st->prod_fills = 0;
   }
   __syncthreads();
   if (st->flag) return;
 
-  if (threadIdx.x >= kConsumerThreads) {
-    if (threadIdx.x == kConsumerThreads) run_producer<B>(p, *st, ring);
+  const int warp = threadIdx.x >> 5;
+  if (warp == kProducerWarp) {
+    if ((threadIdx.x & 31) == 0) {
+      Producer pr{p, ring, *st, policy_evict_first()};
+      walk_schedule<B>(p, *st, pr);
+      if (!pr.ok) pr.drain();
+    }
     return;
   }
-  run_consumers<B>(p, *st, ring, xs, comb, qs, kvn);
+  if (warp == kPrefetchWarp) {
+    if ((threadIdx.x & 31) == 0 && p.prefetch_slots > 0) {
+      Prefetcher pf{p, *st};
+      walk_schedule<B>(p, *st, pf);
+    }
+    return;
+  }
+  run_consumers<B>(p, *st, ring, xs, part, comb, qs, kvn, raw, rope);
 }
 
 }  // namespace mk

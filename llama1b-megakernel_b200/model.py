@@ -75,10 +75,10 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
 
     # ------------------------------------------------------------------ misc
     def __del__(self):
-        h = getattr(self, "_handle", None)
+        h = self.__dict__.get("_handle")
         if h is not None and h.value:
             self.lib.mk_destroy(h)
-            self._handle = ctypes.c_void_p()
+            h.value = None
 
     def new_cache(self, max_seq_len: int | None = None, num_pages: int | None = None) -> PagedKVCache:
         """A fresh cache with this model's geometry (same pool size unless given)."""
@@ -96,9 +96,14 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
     def debug_skip_arrival(self, cta: int) -> None:
         _lib.check(self.lib.mk_debug_skip_arrival(self._handle, int(cta)))
 
+    def set_prefetch(self, lead_slots: int, gbytes_per_s: float = 0.0) -> None:
+        """L2 prefetch of the weight stream: lead in 16 KB fills (0 = off) and
+        the whole grid's paced rate in GB/s (0 = unpaced)."""
+        _lib.check(self.lib.mk_set_prefetch(self._handle, int(lead_slots), float(gbytes_per_s)))
+
     def set_trace(self, enable: bool = True) -> torch.Tensor | None:
         """Record the phase trace of every later launch into a device buffer
-        (int64, [grid, num_layers * 5 + 1, 8]; see ``mk_set_trace``), or stop."""
+        (int64, [grid, num_layers * 5 + 1, 12]; see ``mk_set_trace``), or stop."""
         need = ctypes.c_int64()
         if not enable:
             _lib.check(self.lib.mk_set_trace(self._handle, None, 0, ctypes.byref(need)))
@@ -109,7 +114,7 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         buf = torch.zeros(need.value, dtype=torch.int64, device=self.device)
         _lib.check(self.lib.mk_set_trace(self._handle, buf.data_ptr(), buf.numel(),
                                          ctypes.byref(need)))
-        self._trace = buf.view(grid, self.cfg.num_layers * 5 + 1, 8)
+        self._trace = buf.view(grid, self.cfg.num_layers * 5 + 1, 12)
         return self._trace
 
     def _kv_struct(self, kv: PagedKVCache) -> _lib.MkKVCache:

@@ -13,6 +13,7 @@ import numpy as np
 
 PHASES = ("qkv", "attn", "o", "gu", "down")
 WAIT_START, WAIT_DONE, ROWS, DONE, CONS_STALL, PROD_START, PROD_STALL, PROD_END = range(8)
+ATTN_Q, ATTN_CHUNKS, ATTN_ARRIVE, ATTN_MERGED = range(8, 12)
 
 
 def phase_table(trace, num_layers: int, skip_first_layer: bool = True) -> dict:
@@ -20,7 +21,7 @@ def phase_table(trace, num_layers: int, skip_first_layer: bool = True) -> dict:
     barrier (last arrival -> first release), activation load, consumption
     (median and slowest CTA), and the stall totals accumulated in the phase.
 
-    ``trace``: [grid, num_layers * 5 + 1, 8] int64 (one launch)."""
+    ``trace``: [grid, num_layers * 5 + 1, 12] int64 (one launch)."""
     t = np.asarray(trace, dtype=np.int64).astype(np.float64)
     n_ph = num_layers * 5 + 1
     assert t.shape[1] == n_ph, t.shape
@@ -68,3 +69,28 @@ def format_table(summary: dict) -> str:
         lines.append(f"{name:6s} " + " ".join(f"{r[k]:15.2f}" for k in keys))
     lines.append(f"total {summary['total_us']:.1f} us")
     return "\n".join(lines)
+
+
+def attention_breakdown(trace, num_layers: int) -> dict:
+    """Attention sub-steps (us, mean over layers 1..L-1 of the median / max
+    over the CTAs that had an item): q load, chunk reduction, split
+    arrival, and the last split's merge."""
+    t = np.asarray(trace, dtype=np.int64).astype(np.float64)
+    keys = {"q_load": (WAIT_DONE, ATTN_Q), "chunks": (ATTN_Q, ATTN_CHUNKS),
+            "arrive": (ATTN_CHUNKS, ATTN_ARRIVE), "merge": (ATTN_ARRIVE, ATTN_MERGED)}
+    out = {k: [0.0, 0.0] for k in keys}
+    n = 0
+    for l in range(1, num_layers):
+        ph = l * 5 + 1
+        busy = t[:, ph, ATTN_Q] > 0
+        if not busy.any():
+            continue
+        n += 1
+        for k, (a, b) in keys.items():
+            sel = busy & (t[:, ph, b] > 0)
+            if not sel.any():
+                continue
+            d = (t[sel, ph, b] - t[sel, ph, a]) / 1e3
+            out[k][0] += float(np.median(d))
+            out[k][1] += float(d.max())
+    return {k: (v[0] / max(n, 1), v[1] / max(n, 1)) for k, v in out.items()}
