@@ -154,15 +154,6 @@ int mk_set_timeout_ns(MkModel* m, uint64_t ns);
 int mk_debug_skip_arrival(MkModel* m, int32_t cta);
 
 /*
- * L2 prefetch of the weight stream: each CTA's prefetch lane runs at most
- * `lead_slots` 16 KB ring fills ahead of its bulk-copy producer, paced so the
- * whole grid issues `gbytes_per_s` (0 = unpaced); lead_slots 0 turns it off
- * (the default). No counterpart in the reference (the Neuron compiler
- * schedules its own DMA prefetch, transformer_llama.py:117-122).
- */
-int mk_set_prefetch(MkModel* m, int32_t lead_slots, float gbytes_per_s);
-
-/*
  * Phase trace, off by default (no counterpart in the reference; it plays the
  * role of the reference's profiler captures, main.py:377-407). With a device
  * buffer of at least *needed uint64 entries, every later launch records, per

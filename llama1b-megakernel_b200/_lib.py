@@ -23,7 +23,7 @@ STATUS_NAMES = {
 # Every symbol include/mk.h declares (checked by tests/test_abi.py).
 EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_hidden", "mk_sync",
-    "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_prefetch", "mk_set_trace",
+    "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_last_error", "mk_destroy",
 )
 
@@ -80,7 +80,6 @@ def load() -> ctypes.CDLL:
     lib.mk_sync.argtypes = [VP, VP]
     lib.mk_set_timeout_ns.argtypes = [VP, ctypes.c_uint64]
     lib.mk_debug_skip_arrival.argtypes = [VP, I32]
-    lib.mk_set_prefetch.argtypes = [VP, I32, ctypes.c_float]
     lib.mk_set_trace.argtypes = [VP, VP, ctypes.c_int64, P(ctypes.c_int64)]
     lib.mk_query.argtypes = [VP, P(I32), P(I32), P(I32)]
     lib.mk_last_error.argtypes = []

@@ -49,8 +49,6 @@ struct MkModel {
   int smem = 0;
   int kmax = 0;
   int part_cap = 0;
-  int prefetch_slots = 0;
-  float prefetch_gbs = 0.f;
   bool has_weights = false;
   MkWeights w{};
   unsigned long long timeout_ns = 2000000000ull;
@@ -181,8 +179,6 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   p.nseg_qd = mk::pieces_per_row(c.num_q_heads * 64);
   p.nseg_i = mk::pieces_per_row(c.intermediate);
   p.part_cap = m->part_cap;
-  p.prefetch_slots = m->prefetch_slots;
-  p.prefetch_ns_per_byte = m->prefetch_gbs > 0.f ? (float)m->grid / m->prefetch_gbs : 0.f;
   p.mode = mode;
   p.flags = flags;
   p.embed = static_cast<const mk::bf16*>(m->w.embed);
@@ -410,16 +406,6 @@ int mk_set_timeout_ns(MkModel* m, uint64_t ns) {
 int mk_debug_skip_arrival(MkModel* m, int32_t cta) {
   if (!m) return fail(MK_EINVAL, "model is NULL");
   m->debug_skip_cta = cta;
-  return MK_OK;
-}
-
-int mk_set_prefetch(MkModel* m, int32_t lead_slots, float gbytes_per_s) {
-  if (!m) return fail(MK_EINVAL, "model is NULL");
-  if (lead_slots < 0 || lead_slots > 4096)
-    return fail(MK_EINVAL, "prefetch lead %d outside [0, 4096]", lead_slots);
-  if (!(gbytes_per_s >= 0.f)) return fail(MK_EINVAL, "prefetch rate must be >= 0");
-  m->prefetch_slots = lead_slots;
-  m->prefetch_gbs = gbytes_per_s;
   return MK_OK;
 }
 

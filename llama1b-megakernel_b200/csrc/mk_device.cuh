@@ -14,16 +14,21 @@ namespace mk {
 constexpr int kHeadDim = 64;
 constexpr int kGroup = 4;                  // q heads per kv head
 constexpr int kSlotBytes = 16384;          // one ring slot
-constexpr int kConsumerWarps = 16;
+// 14 consumer + 2 producer warps: 16 warps keep 128 registers per thread
+// (the register file is split over four schedulers, 16K registers each).
+constexpr int kConsumerWarps = 14;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kAttnWarps = 8;              // consumer warps that work on attention chunks
-constexpr int kProducerWarp = kConsumerWarps;      // lane 0 issues the ring copies
-constexpr int kPrefetchWarp = kConsumerWarps + 1;  // lane 0 issues L2 prefetches ahead of it
-constexpr int kThreads = kConsumerThreads + 64;
+constexpr int kAttnWarps = 8;              // warp states kept for the attention merge
+// Ring copies are issued by kProducers lanes (lane 0 of warps kConsumerWarps
+// .. + kProducers - 1), producer k taking the fills f with f % kProducers == k:
+// one lane issues at most ~50 GB/s of 16 KB bulk copies.
+constexpr int kProducers = 2;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kThreads = kConsumerThreads + kProducers * 32;
 constexpr int kSegCols = 2048;             // max columns of one piece (a row segment)
 constexpr int kAttnChunk = 64;             // cached positions per attention slot
 constexpr int kMaxSplit = 32;              // split-K pieces per (sequence, kv head)
-constexpr int kSplitMinPositions = 64;     // no split shorter than this (one chunk)
+constexpr int kSplitMinPositions = 512;    // no split shorter than this (8 chunks)
 constexpr int kPartialStride = kHeadDim + 2;  // o[64], m, l per q head
 
 // Device error codes (error word [0]).
@@ -115,11 +120,6 @@ __device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint
       " [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
-}
-
-// Warm L2 with [src, src + bytes) without waiting (16-byte aligned, multiple of 16).
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // 128-bit shared-memory load at a shared-window address. volatile: it must stay

@@ -4,22 +4,19 @@
 // sequences through every decoder layer, then the final norm, the tied
 // lm_head and a greedy argmax.
 //
-// CTA = 16 consumer warps + 1 producer warp + 1 prefetch warp.
+// CTA = 14 consumer warps + 2 producer warps.
 //
-// * The producer (one lane) walks the CTA's whole schedule of HBM reads for
+// * The producers (lane 0 of two warps, alternating fills: one lane issues
+//   at most ~50 GB/s of 16 KB bulk copies) walk the CTA's whole schedule of HBM reads for
 //   the step — its slice of every weight matrix of every layer, its KV-cache
 //   chunks, its lm_head rows — and streams them with bulk copies
 //   (cp.async.bulk, the TMA engine without a tensor map) into a ring of 16 KB
 //   shared-memory slots, each guarded by a full/empty mbarrier pair. Weights
 //   and cached K/V do not depend on activations, so the producer never waits
 //   for a grid barrier: it runs ahead by the ring's depth (~190 KB per SM).
-// * The prefetch lane walks the same schedule a configurable number of slots
-//   ahead of the producer and warms L2 with cp.async.bulk.prefetch.L2, so the
-//   stream keeps HBM busy through grid barriers and the attention phase, and
-//   the producer refills freed slots from L2.
 // * The consumers walk the same schedule. Every streamed row is cut into
 //   pieces of at most 2048 columns (4 KB); piece q of a phase goes to warp
-//   q mod 16, so each slot is read by four warps at once, each with 128-bit
+//   q mod 14, so each slot is read by four warps at once, each with 128-bit
 //   shared loads. A warp keeps its 2048-column segment of the activation
 //   vector in registers as packed bf16 and accumulates with mixed-precision
 //   fma.rn.f32.bf16 into four independent fp32 chains, then reduces across
@@ -68,8 +65,6 @@ struct Params {
   int flags;
   int nseg_h, nseg_qd, nseg_i;  // pieces per row for K = H, NQ*64, I
   int part_cap;                 // floats in the shared partial-sum array
-  int prefetch_slots;           // L2 prefetch lead over the producer, in slots (0 = off)
-  float prefetch_ns_per_byte;   // pacing of the L2 prefetch (0 = unpaced)
   // weights (packed, see mk.h)
   const bf16* embed;
   const bf16* w_qkv;
@@ -137,8 +132,7 @@ struct SmemState {
   int pos[4];
   int n_split;
   int flag;
-  uint32_t prod_fills;  // ring fills the producer has issued (read by the prefetch lane)
-  int pad[5];
+  int pad[6];
   float red[kConsumerWarps * 4];
   float am_val[kConsumerWarps * 4];
   int am_idx[kConsumerWarps * 4];
@@ -276,7 +270,7 @@ __device__ __forceinline__ AttnItem attn_item(const Params& p, const SmemState& 
 // Walk the CTA's streaming schedule for one step, in the order the consumers
 // use it: per layer the QKV rows, the KV chunks of its attention items, the
 // o_proj rows, the gate/up row pairs, the down rows; then the lm_head rows.
-// `ops` is the producer (bulk copies into the ring) or the prefetch lane.
+// `ops` is a producer (bulk copies into the ring).
 template <int B, class Ops>
 __device__ void walk_schedule(const Params& p, const SmemState& st, Ops& ops) {
   Sched sch;
@@ -322,6 +316,18 @@ struct Ring {
   int S;
   uint32_t n = 0;  // fills seen so far (the same count on every side)
   unsigned long long stall_ns = 0;  // time spent waiting (traced runs only)
+};
+
+// Noinline phase functions take the caller's Ring by reference but work on a
+// register copy (a reference into the caller's stack would turn every access
+// into a local-memory round trip); this writes the counters back on exit.
+struct RingWriteBack {
+  Ring& dst;
+  const Ring& src;
+  __device__ ~RingWriteBack() {
+    dst.n = src.n;
+    dst.stall_ns = src.stall_ns;
+  }
 };
 
 // Slow path of a consumer warp's wait for a fill: every lane polls the
@@ -374,7 +380,10 @@ struct Producer {
   Ring& r;
   SmemState& st;
   uint64_t pol;
+  int k;  // this producer takes the fills f with f % kProducers == k
   bool ok = true;
+
+  __device__ bool mine() const { return (int)(r.n % kProducers) == k; }
 
   // Claim the next slot for `bytes` of transfers; nullptr when aborting.
   __device__ uint8_t* begin(uint32_t bytes) {
@@ -393,13 +402,10 @@ struct Producer {
     return r.slots + (size_t)slot * kSlotBytes;
   }
   __device__ uint64_t* bar() { return &r.full[r.n % r.S]; }
-  __device__ void end() {
-    r.n++;
-    *reinterpret_cast<volatile uint32_t*>(&st.prod_fills) = r.n;
-  }
+  __device__ void end() { r.n++; }
 
   __device__ void mark(int ph, bool start) {
-    if (!p.trace) return;
+    if (!p.trace || k != 0) return;
     if (start) {
       trace_put(p, ph, kTrProdStart, global_ns());
     } else {
@@ -413,6 +419,10 @@ struct Producer {
     const int ups = units_per_slot(unit_bytes);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(base);
     for (int u = sp.u0; u < sp.u1 && ok; u += ups) {
+      if (!mine()) {
+        r.n++;
+        continue;
+      }
       const int n = min(ups, sp.u1 - u);
       const uint32_t bytes = (uint32_t)n * unit_bytes;
       uint8_t* dst = begin(bytes);
@@ -425,6 +435,10 @@ struct Producer {
   // Stream cached K and V rows [c0, c0 + n) of (seq b, kv head g), n <= 64,
   // K into the slot's first 8 KB and V into its second.
   __device__ void kv_chunk(int layer, int b, int g, int c0, int n) {
+    if (!mine()) {
+      r.n++;
+      return;
+    }
     uint8_t* dst = begin((uint32_t)n * 2 * kHeadDim * 2);
     if (!dst) return;
     const int ps = p.page_size;
@@ -456,86 +470,9 @@ struct Producer {
   // so no bulk copy is still writing shared memory when the CTA exits.
   __device__ void drain() {
     const uint32_t first = r.n > (uint32_t)r.S ? r.n - r.S : 0;
-    for (uint32_t k = first; k < r.n; ++k) {
-      mbar_wait(p, &r.full[k % r.S], (k / r.S) & 1, -1, 2 * p.timeout_ns);
+    for (uint32_t f = first; f < r.n; ++f) {
+      if ((int)(f % kProducers) == k) mbar_wait(p, &r.full[f % r.S], (f / r.S) & 1, -1, 2 * p.timeout_ns);
     }
-  }
-};
-
-// The prefetch lane: the producer's schedule as L2 prefetches, at most
-// `prefetch_slots` fills ahead of it and paced to a fixed byte rate, so HBM
-// keeps streaming while the consumers sit in barriers or attention, without
-// flooding the memory system with requests (which would delay the
-// latency-bound barrier and activation traffic). Nothing waits for a
-// prefetch, so on any failure the lane just stops.
-struct Prefetcher {
-  const Params& p;
-  const SmemState& st;
-  uint32_t n = 0;
-  bool ok = true;
-  uint64_t t_next = 0;  // earliest globaltimer ns for the next prefetch
-
-  // Fill n may be prefetched once the producer has issued fill n - lead and
-  // the pacing clock allows it.
-  __device__ bool gate() {
-    const uint32_t lead = (uint32_t)p.prefetch_slots;
-    uint64_t t0 = 0;
-    for (uint32_t it = 0;; ++it) {
-      const uint32_t prod = *reinterpret_cast<const volatile uint32_t*>(&st.prod_fills);
-      if (n < prod + lead && (t_next == 0 || global_ns() >= t_next)) return true;
-      if ((it & 15) == 15) {
-        if (aborted(p)) return false;
-        const uint64_t now = global_ns();
-        if (t0 == 0) {
-          t0 = now;
-        } else if (now - t0 > p.timeout_ns) {
-          return false;
-        }
-      }
-      __nanosleep(64);
-    }
-  }
-  __device__ void mark(int, bool) {}
-
-  __device__ void pace(uint32_t bytes) {
-    if (p.prefetch_ns_per_byte > 0.f) {
-      const uint64_t now = global_ns();
-      const uint64_t base = (t_next > now || t_next == 0) ? (t_next ? t_next : now) : now;
-      t_next = base + (uint64_t)(bytes * p.prefetch_ns_per_byte);
-    }
-  }
-
-  __device__ void units(const bf16* base, int unit_bytes, Split sp) {
-    const int ups = units_per_slot(unit_bytes);
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(base);
-    for (int u = sp.u0; u < sp.u1 && ok; u += ups) {
-      const int k = min(ups, sp.u1 - u);
-      if (!(ok = gate())) return;
-      prefetch_l2(src + (size_t)u * unit_bytes, (uint32_t)k * unit_bytes);
-      pace((uint32_t)k * unit_bytes);
-      n++;
-    }
-  }
-
-  __device__ void kv_chunk(int layer, int b, int g, int c0, int cnt) {
-    if (!(ok = gate())) return;
-    const int ps = p.page_size;
-    const size_t layer_off = (size_t)layer * p.num_pages * p.NKV * ps * kHeadDim;
-    for (int q = c0; q < c0 + cnt;) {
-      const int off = q % ps;
-      const int run = min(c0 + cnt - q, ps - off);
-      const int page = __ldg(p.block_tables + b * p.max_blocks + q / ps);
-      if (page < 0 || page >= p.num_pages) {
-        ok = false;  // the producer reports it
-        return;
-      }
-      const size_t src_off = layer_off + (((size_t)page * p.NKV + g) * ps + off) * kHeadDim;
-      prefetch_l2(p.k_pages + src_off, (uint32_t)run * kHeadDim * 2);
-      prefetch_l2(p.v_pages + src_off, (uint32_t)run * kHeadDim * 2);
-      q += run;
-    }
-    pace((uint32_t)cnt * kHeadDim * 4);
-    n++;
   }
 };
 
@@ -629,24 +566,23 @@ __device__ __forceinline__ float dot8(const uint4& w, const float (&x)[8], float
 // One streamed GEMV phase over units [sp.u0, sp.u1): each unit is
 // `rows_per_unit` rows of K bf16 columns, cut into pieces of K / nseg
 // columns. Work items are groups of `grp` consecutive pieces (1, or a whole
-// row when the caller needs full-row sums); item t goes to warp t mod 16.
+// row when the caller needs full-row sums); item t goes to warp t mod 14.
 // The warp reduces its item against the B activation rows in shared memory
 // (kept in registers for B == 1) and calls out(t, sums, lane) with the fp32
 // sums valid in every lane.
 template <int B, class Out>
 __device__ __noinline__ bool gemv_phase(const Params& p, Ring& ring_io, uint32_t xs_s, int K,
                                         int nseg, int rows_per_unit, int grp, Split sp, int where,
-                                        Out&& out) {
+                                        Out& out_io) {
   constexpr int NC = kConsumerWarps;
   Ring ring = ring_io;  // registers for the loop; written back on every exit
-  struct WriteBack {
-    Ring& dst;
-    const Ring& src;
-    __device__ ~WriteBack() {
-      dst.n = src.n;
-      dst.stall_ns = src.stall_ns;
-    }
-  } wb{ring_io, ring};
+  RingWriteBack wb{ring_io, ring};
+  Out out = out_io;  // likewise the output functor's state
+  struct OutWriteBack {
+    Out& dst;
+    const Out& src;
+    __device__ ~OutWriteBack() { dst = src; }
+  } owb{out_io, out};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seg = K / nseg;
   const int CH = seg >> 8;
@@ -770,20 +706,44 @@ __device__ __noinline__ void merge_group(const Params& p, int b, int g, int ns, 
   }
 }
 
+// Online-softmax merge of another (m, l, o[8]) state into this lane's.
+__device__ __forceinline__ void softmax_merge(float& m, float& l, float (&o)[8], float m2, float l2,
+                                              const float (&o2)[8]) {
+  const float M = fmaxf(m, m2);
+  if (M == -INFINITY) return;
+  const float a1 = (m == -INFINITY) ? 0.f : __expf(m - M);
+  const float a2 = (m2 == -INFINITY) ? 0.f : __expf(m2 - M);
+  l = l * a1 + l2 * a2;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = o[e] * a1 + o2[e] * a2;
+  m = M;
+}
+
+// Split-K GQA flash-decode for the CTA's items. A 64-position chunk is spread
+// over the consumer warps, four positions at a time: lane (h, j) of a warp
+// scores position 4w + j/2 against q head h over half of the head dims (the
+// other half on lane j^1), with q kept in registers as packed bf16, then
+// accumulates dims [8j, 8j + 8) of P.V. Warp states are merged in shared
+// memory; a single split writes the heads' output itself, several splits
+// leave partials for the last one to merge.
 template <int B>
-__device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int layer,
-                                float* comb, bf16* qs, float* kvn) {
+__device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, SmemState& st,
+                                             int layer, float* comb, bf16* qs, float* kvn) {
+  constexpr int NC = kConsumerWarps;
+  Ring ring = ring_io;
+  RingWriteBack wb{ring_io, ring};
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool attn_warp = warp < kAttnWarps;
   const int NQKV = p.NQ + 2 * p.NKV;
-  const int T = B * p.NKV * st.n_split;
+  const int ns = st.n_split;
+  const int T = B * p.NKV * ns;
   const float scale = 0.125f;  // head_dim ** -0.5
   const int h = lane >> 3, j = lane & 7;
+  const int pp = j >> 1, half = j & 1;
   for (int it = blockIdx.x; it < T; it += gridDim.x) {
     const AttnItem a = attn_item(p, st, it);
     consumer_sync();
-    // q of the group's heads, and the new token's own K and V row (used by
-    // the last split's merge), in one round trip.
+    // q of the group's heads, and the new token's own K and V row, in one
+    // round trip.
     if (tid < kGroup * kHeadDim / 8) {
       reinterpret_cast<uint4*>(qs)[tid] =
           __ldcg(reinterpret_cast<const uint4*>(p.qkv + ((size_t)a.b * NQKV + a.g * kGroup) * kHeadDim) + tid);
@@ -799,58 +759,60 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
     }
     consumer_sync();
     if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnQ, global_ns());
+    uint4 qh[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) qh[c] = reinterpret_cast<const uint4*>(qs + h * kHeadDim + half * 32)[c];
     float m = -INFINITY, l = 0.f, o[8];
     bool fail = false;
 #pragma unroll
     for (int e = 0; e < 8; ++e) o[e] = 0.f;
-    const uint4* q4 = reinterpret_cast<const uint4*>(qs + h * kHeadDim);
     for (int c0 = a.p0; c0 < a.p1; c0 += kAttnChunk) {
       const int n = min(kAttnChunk, a.p1 - c0);
+      const int nw = min(NC, (n + 3) >> 2);  // warps with positions in this chunk
       const uint32_t f = ring.n++;
-      if (!attn_warp || fail) continue;
+      if (fail || warp >= nw) continue;
       if (!ring_wait(p, ring, f, 200 + layer)) {
         fail = true;
         continue;
       }
       const uint8_t* slot = ring.slots + (size_t)(f % ring.S) * kSlotBytes;
-      const int pc = warp * 8 + j;
-      const bool valid = pc < n;
-      float sc = -INFINITY;
-      if (valid) {
-        const uint4* k4 = reinterpret_cast<const uint4*>(slot + pc * kHeadDim * 2);
-        float acc = 0.f;
+      const uint8_t* vbase = slot + 8192;
+      for (int base = warp * 4; base < n; base += NC * 4) {
+        const int pc = base + pp;
+        const bool valid = pc < n;
+        float sc = -INFINITY;
+        if (valid) {
+          const uint4* k4 = reinterpret_cast<const uint4*>(slot + pc * kHeadDim * 2 + half * 64);
+          float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int c = (e + j) & 7;
-          float qf[8];
-          unpack8(q4[c], qf);
-          acc = dot8(k4[c], qf, acc);
+          for (int c = 0; c < 4; ++c) {
+            const uint4 kw = k4[c];
+            fma2_bf16(kw.x, qh[c].x, s0, s1);
+            fma2_bf16(kw.y, qh[c].y, s0, s1);
+            fma2_bf16(kw.z, qh[c].z, s0, s1);
+            fma2_bf16(kw.w, qh[c].w, s0, s1);
+          }
+          sc = s0 + s1;
         }
-        sc = acc * scale;
-      }
-      float cmax = sc;
-      cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
-      cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
-      cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 4));
-      // Warp-uniform: does this warp own any position of the chunk?
-      if (warp * 8 < n) {
+        sc += __shfl_xor_sync(0xffffffffu, sc, 1);  // the two halves of the dot
+        sc *= scale;
+        float cmax = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 2));
+        cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 4));
         const float m_new = fmaxf(m, cmax);
         const float alpha = (m == -INFINITY) ? 0.f : __expf(m - m_new);
-        const float pe = (valid && m_new > -INFINITY) ? __expf(sc - m_new) : 0.f;
-        float ps = pe;
+        const float pe = valid ? __expf(sc - m_new) : 0.f;
+        float ps = half == 0 ? pe : 0.f;
         ps += __shfl_xor_sync(0xffffffffu, ps, 1);
         ps += __shfl_xor_sync(0xffffffffu, ps, 2);
         ps += __shfl_xor_sync(0xffffffffu, ps, 4);
         l = l * alpha + ps;
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] *= alpha;
-        const uint8_t* vbase = slot + 8192;
 #pragma unroll
-        for (int pp = 0; pp < 8; ++pp) {
-          const float pv = __shfl_sync(0xffffffffu, pe, (lane & ~7) | pp);
-          if (warp * 8 + pp < n) {
-            const uint4 vv =
-                reinterpret_cast<const uint4*>(vbase + (warp * 8 + pp) * kHeadDim * 2)[j];
+        for (int q = 0; q < 4; ++q) {
+          const float pv = __shfl_sync(0xffffffffu, pe, (lane & ~7) | (q * 2));
+          if (base + q < n) {
+            const uint4 vv = reinterpret_cast<const uint4*>(vbase + (base + q) * kHeadDim * 2)[j];
             float vf[8];
             unpack8(vv, vf);
 #pragma unroll
@@ -859,14 +821,14 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
         }
         m = m_new;
       }
-      ring_release(ring, f, warp == 0 ? (uint32_t)(kConsumerWarps - kAttnWarps + 1) : 1u);
+      ring_release(ring, f, warp == 0 ? (uint32_t)(NC - nw + 1) : 1u);
     }
     // Split 0 also takes the new token's own K/V (the "active slot"), on
     // warp 0: lane (h, j) adds dims [8j, 8j + 8) of q_h . k_new, reduced
     // over the head's eight lanes.
     if (a.s == 0 && warp == 0) {
       float qf[8];
-      unpack8(q4[j], qf);
+      unpack8(reinterpret_cast<const uint4*>(qs + h * kHeadDim)[j], qf);
       float sa = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) sa = fmaf(qf[e], kvn[j * 8 + e], sa);
@@ -883,17 +845,32 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
       m = m_new;
     }
     if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnChunks, global_ns());
-    // Merge the attention warps' (m, l, o) for each q head of the group.
-    if (attn_warp) {
-      float* cw = comb + (warp * kGroup + h) * kPartialStride;
+    if (consumer_any(fail)) return false;
+    // Merge the warps' states: warps 8.. into 0.. through shared memory,
+    // then 0..7 into one state per (head, dim).
+    auto put = [&](int w) {
+      float* cw = comb + (w * kGroup + h) * kPartialStride;
 #pragma unroll
       for (int e = 0; e < 8; ++e) cw[j * 8 + e] = o[e];
       if (j == 0) {
         cw[kHeadDim] = m;
         cw[kHeadDim + 1] = l;
       }
+    };
+    if (warp >= kAttnWarps) put(warp - kAttnWarps);
+    consumer_sync();
+    if (warp + kAttnWarps < NC) {
+      const float* cw = comb + (warp * kGroup + h) * kPartialStride;
+      float o2[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o2[e] = cw[j * 8 + e];
+      softmax_merge(m, l, o, cw[kHeadDim], cw[kHeadDim + 1], o2);
     }
-    if (consumer_any(fail)) return false;
+    consumer_sync();
+    if (warp < kAttnWarps) put(warp);
+    consumer_sync();
+    static_assert(kConsumerWarps >= kAttnWarps && kConsumerWarps <= 2 * kAttnWarps,
+                  "attention merge assumes kAttnWarps <= warps <= 2 * kAttnWarps");
     if (tid < kGroup * kHeadDim) {
       const int hh = tid >> 6, d = tid & 63;
       float M = -INFINITY;
@@ -913,27 +890,39 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
           }
         }
       }
-      float* pp = p.partials +
-                  ((((size_t)a.b * p.NKV + a.g) * kMaxSplit + a.s) * kGroup + hh) * kPartialStride;
-      pp[d] = O;
-      if (d == 0) {
-        pp[kHeadDim] = M;
-        pp[kHeadDim + 1] = L;
+      if (ns == 1) {
+        // The only split (it holds the active slot, so L > 0): final output.
+        p.attn[(size_t)a.b * p.NQ * kHeadDim + (a.g * kGroup + hh) * kHeadDim + d] = f2bf(O / L);
+      } else {
+        float* pp2 = p.partials +
+                     ((((size_t)a.b * p.NKV + a.g) * kMaxSplit + a.s) * kGroup + hh) * kPartialStride;
+        pp2[d] = O;
+        if (d == 0) {
+          pp2[kHeadDim] = M;
+          pp2[kHeadDim + 1] = L;
+        }
       }
     }
     consumer_sync();
+    if (ns == 1) {
+      if (tid == 0) {
+        red_release_add_u32(p.counters + kCntHeadsDone, 1u);
+        if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
+      }
+      continue;
+    }
     // Count the split; the last one of its (seq, kv head) merges them all.
     if (tid == 0) {
       uint32_t* arr = p.counters + kCntArrive + a.b * p.NKV + a.g;
       const uint32_t old = atom_add_acq_rel_u32(arr, 1u);
-      const int last = (old == (uint32_t)(st.n_split - 1)) ? 1 : 0;
+      const int last = (old == (uint32_t)(ns - 1)) ? 1 : 0;
       if (last) atomicExch(arr, 0u);
       st.flag = last;
       if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
     }
     consumer_sync();
     if (st.flag) {
-      merge_group(p, a.b, a.g, st.n_split, comb);
+      merge_group(p, a.b, a.g, ns, comb);
       consumer_sync();
       if (tid == 0) {
         red_release_add_u32(p.counters + kCntHeadsDone, 1u);
@@ -943,6 +932,40 @@ __device__ bool attention_phase(const Params& p, Ring& ring, SmemState& st, int 
   }
   return true;
 }
+
+// GEMV phase output: one fp32 partial per piece, into shared memory.
+template <int B>
+struct ToPart {
+  float* part;
+  __device__ void operator()(int q, const float (&v)[B], int lane) const {
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < B; ++b) part[q * B + b] = v[b];
+    }
+  }
+};
+
+// lm_head output: optional fp32 logits and this warp's running greedy
+// argmax (lowest index on ties), kept by lane 0.
+template <int B>
+struct LmOut {
+  float* logits;
+  int V, u0;
+  float best_v[B];
+  int best_i[B];
+  __device__ void operator()(int t, const float (&v)[B], int lane) {
+    if (lane != 0) return;
+    const int u = u0 + t;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (logits) logits[(size_t)b * V + u] = v[b];
+      if (v[b] > best_v[b] || (v[b] == best_v[b] && u < best_i[b])) {
+        best_v[b] = v[b];
+        best_i[b] = u;
+      }
+    }
+  }
+};
 
 template <int B>
 __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* xs, float* part,
@@ -970,12 +993,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
     }
   };
   // Phase-local partial sums: part[piece * B + b].
-  auto to_part = [&](int q, float (&v)[B], int lane) {
-    if (lane == 0) {
-#pragma unroll
-      for (int b = 0; b < B; ++b) part[q * B + b] = v[b];
-    }
-  };
+  ToPart<B> to_part{part};
   // Sum of a row's nseg pieces (fixed order).
   auto row_sum = [&](int q0, int nseg, int b) {
     float s = part[q0 * B + b];
@@ -1154,36 +1172,23 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       load_rows<B>(src, H, p.norm_final, p.eps, xs, p.kmax, st);
     }
     mark(p.L * 5, kTrRowsLoaded);
-    float best_v[B];
-    int best_i[B];
+    const Split sl = sch.next(p.V);
+    LmOut<B> lm{p.logits, p.V, sl.u0};
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      best_v[b] = -INFINITY;
-      best_i[b] = 0x7fffffff;
+      lm.best_v[b] = -INFINITY;
+      lm.best_i[b] = 0x7fffffff;
     }
-    const Split sl = sch.next(p.V);
     // One item per lm_head row (all its pieces), so the warp has the logit.
-    const bool ok = gemv_phase<B>(p, ring, xs_s, H, p.nseg_h, 1, p.nseg_h, sl, 11000,
-                                  [&](int t, float (&v)[B], int lane) {
-      if (lane != 0) return;
-      const int u = sl.u0 + t;
-#pragma unroll
-      for (int b = 0; b < B; ++b) {
-        if (p.logits) p.logits[(size_t)b * p.V + u] = v[b];
-        if (v[b] > best_v[b] || (v[b] == best_v[b] && u < best_i[b])) {
-          best_v[b] = v[b];
-          best_i[b] = u;
-        }
-      }
-    });
+    const bool ok = gemv_phase<B>(p, ring, xs_s, H, p.nseg_h, 1, p.nseg_h, sl, 11000, lm);
     if (consumer_any(!ok)) return;
     mark_done(p.L * 5);
     const int lane = tid & 31, w = tid >> 5;
     if (lane == 0) {
 #pragma unroll
       for (int b = 0; b < B; ++b) {
-        st.am_val[w * B + b] = best_v[b];
-        st.am_idx[w * B + b] = best_i[b];
+        st.am_val[w * B + b] = lm.best_v[b];
+        st.am_idx[w * B + b] = lm.best_i[b];
       }
     }
     consumer_sync();
@@ -1283,24 +1288,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     ns = max(1, min(ns, (pmax + kSplitMinPositions - 1) / kSplitMinPositions));
     st->n_split = ns;
     st->flag = bad ? 1 : 0;
-    st->prod_fills = 0;
   }
   __syncthreads();
   if (st->flag) return;
 
   const int warp = threadIdx.x >> 5;
-  if (warp == kProducerWarp) {
+  if (warp >= kProducerWarp && warp < kProducerWarp + kProducers) {
     if ((threadIdx.x & 31) == 0) {
-      Producer pr{p, ring, *st, policy_evict_first()};
+      Producer pr{p, ring, *st, policy_evict_first(), warp - kProducerWarp};
       walk_schedule<B>(p, *st, pr);
       if (!pr.ok) pr.drain();
-    }
-    return;
-  }
-  if (warp == kPrefetchWarp) {
-    if ((threadIdx.x & 31) == 0 && p.prefetch_slots > 0) {
-      Prefetcher pf{p, *st};
-      walk_schedule<B>(p, *st, pf);
     }
     return;
   }

@@ -96,11 +96,6 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
     def debug_skip_arrival(self, cta: int) -> None:
         _lib.check(self.lib.mk_debug_skip_arrival(self._handle, int(cta)))
 
-    def set_prefetch(self, lead_slots: int, gbytes_per_s: float = 0.0) -> None:
-        """L2 prefetch of the weight stream: lead in 16 KB fills (0 = off) and
-        the whole grid's paced rate in GB/s (0 = unpaced)."""
-        _lib.check(self.lib.mk_set_prefetch(self._handle, int(lead_slots), float(gbytes_per_s)))
-
     def set_trace(self, enable: bool = True) -> torch.Tensor | None:
         """Record the phase trace of every later launch into a device buffer
         (int64, [grid, num_layers * 5 + 1, 12]; see ``mk_set_trace``), or stop."""
