@@ -267,13 +267,15 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   }
   m->num_slots = slots;
   m->smem = mk::smem_bytes_for(slots, B, m->kmax, m->part_cap, cfg->hidden);
+  // The attribute is per kernel, not per handle: allow the device maximum so
+  // handles with different geometries can be used in any order.
   for (int b = 1; b <= 4; ++b) {
     cudaError_t e = cudaSuccess;
     switch (b) {
-      case 1: e = set_smem_b<1>(m->smem); break;
-      case 2: e = set_smem_b<2>(m->smem); break;
-      case 3: e = set_smem_b<3>(m->smem); break;
-      case 4: e = set_smem_b<4>(m->smem); break;
+      case 1: e = set_smem_b<1>(smem_cap); break;
+      case 2: e = set_smem_b<2>(smem_cap); break;
+      case 3: e = set_smem_b<3>(smem_cap); break;
+      case 4: e = set_smem_b<4>(smem_cap); break;
     }
     if (e != cudaSuccess) {
       delete m;
@@ -287,12 +289,6 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
     return fail(MK_ECUDA, "kernel does not fit one CTA per SM (%s)", cudaGetErrorString(e));
   }
   m->grid = m->num_sms;
-  // The o_proj prologue keeps one (m, l) pair per attention item (at most one
-  // item per CTA, four heads each) in the attention scratch.
-  if (8 * m->grid * 4 > mk::kAttnWarps * mk::kGroup * mk::kPartialStride * 4) {
-    delete m;
-    return fail(MK_EINVAL, "grid of %d CTAs exceeds the attention scratch", m->grid);
-  }
 
   // Scratch: one allocation, 256-byte aligned sub-buffers.
   const size_t H = cfg->hidden, I = cfg->intermediate, NQ = cfg->num_q_heads,

@@ -665,6 +665,8 @@ __device__ __forceinline__ bool grid_wait(const Params& p, uint32_t* counter, ui
 
 static_assert(kConsumerThreads >= kGroup * kHeadDim + kGroup * kMaxSplit,
               "merge_group needs a thread per (head, dim) plus one per (head, split)");
+static_assert(kGroup * kMaxSplit * 2 <= kAttnWarps * kGroup * kPartialStride,
+              "merge_group keeps its (m, l) table in the attention scratch");
 
 // The last split to finish a (seq b, kv head g) merges every split's
 // (m, l, o) — split 0 already holds the new token's own K/V — and writes the
