@@ -140,6 +140,33 @@ int mk_decode(MkModel* m, const int32_t* tokens, const int32_t* positions, int32
 int mk_decode_hidden(MkModel* m, const void* hidden_in, const int32_t* positions, int32_t batch,
                      const MkKVCache* kv, void* hidden_out, void* stream);
 
+/*
+ * mk_decode without a handle and without allocating anything, for callers
+ * that cannot call cudaMalloc: a host whose own pool or arena already owns
+ * the device memory (a library-side allocation would fail or fragment it), a
+ * plugin invoked from inside another runtime's allocator or memory-pressure
+ * callback (re-entering the allocator is not allowed there), or a
+ * latency-critical loop that cannot afford cudaMalloc's implicit device
+ * synchronisation. No counterpart in the reference (its scratch is allocated
+ * by the Neuron runtime when the model loads).
+ *
+ * Same arguments and results as mk_decode, but the geometry and weights are
+ * passed in (cfg, w) and the kernel's scratch lives in a 512 KiB array built
+ * into the library (one per GPU, held until the process exits): enough for
+ * Llama-3.2-1B at cfg->max_batch 1; larger geometries return MK_EINVAL and
+ * must use mk_init / mk_decode. Runs on the current device. Its first call on
+ * a device looks up the array's device address and sets the kernels'
+ * shared-memory limit, so make that call before any stream capture. Each call
+ * zeroes the counters it needs first. All calls on a device share the one
+ * array, so calls that overlap on the GPU (other streams, other threads) race:
+ * order them on one stream. Device-side failures are not reported by mk_sync:
+ * pass error_out (device, 4 int32, zeroed by the call; code, detail, CTA,
+ * thread on failure) or NULL.
+ */
+int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tokens,
+                     const int32_t* positions, int32_t batch, const MkKVCache* kv, float* logits,
+                     int32_t* next_ids, int32_t flags, int32_t* error_out, void* stream);
+
 /* Wait for `stream`, then report and clear any device-side error. */
 int mk_sync(MkModel* m, void* stream);
 

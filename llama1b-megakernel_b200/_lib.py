@@ -22,7 +22,7 @@ STATUS_NAMES = {
 
 # Every symbol include/mk.h declares (checked by tests/test_abi.py).
 EXPORTED = (
-    "mk_init", "mk_load_weights", "mk_decode", "mk_decode_hidden", "mk_sync",
+    "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_last_error", "mk_destroy",
 )
@@ -76,6 +76,8 @@ def load() -> ctypes.CDLL:
     lib.mk_init.argtypes = [P(MkConfig), ctypes.c_int, P(VP)]
     lib.mk_load_weights.argtypes = [VP, P(MkWeights)]
     lib.mk_decode.argtypes = [VP, VP, VP, I32, P(MkKVCache), VP, VP, I32, VP]
+    lib.mk_decode_static.argtypes = [P(MkConfig), P(MkWeights), VP, VP, I32, P(MkKVCache), VP, VP,
+                                     I32, VP, VP]
     lib.mk_decode_hidden.argtypes = [VP, VP, VP, I32, P(MkKVCache), VP, VP]
     lib.mk_sync.argtypes = [VP, VP]
     lib.mk_set_timeout_ns.argtypes = [VP, ctypes.c_uint64]

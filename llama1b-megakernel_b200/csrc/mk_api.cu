@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/mk.h"
@@ -219,6 +220,50 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// mk_decode_static: the decode step without a handle and without allocating.
+//
+// Its scratch (residual, q/k/v, attention partials, counters, argmax keys,
+// error words) lives in this file-scope device array instead of a cudaMalloc
+// made by mk_init. Every GPU that loads the library holds one copy until the
+// process exits, and every call on that GPU shares it.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = 512 * 1024;  // enough for Llama-3.2-1B at max_batch 1
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_ptr[kStaticMaxDevices] = {};  // device address of g_static_scratch, per device
+
+// Once per device, with that device current: the array's device address (the
+// host-side name g_static_scratch is only a stand-in and must never reach a
+// kernel) and the kernels' shared-memory limit.
+int static_setup(int device, void** out) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (device < 0 || device >= kStaticMaxDevices)
+    return fail(MK_EINVAL, "device %d beyond the %d devices mk_decode_static supports", device,
+                kStaticMaxDevices);
+  if (!g_static_ptr[device]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(MK_ECUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+    int cap = 0;
+    MK_CUDA(cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    MK_CUDA(set_smem_b<1>(cap));
+    MK_CUDA(set_smem_b<2>(cap));
+    MK_CUDA(set_smem_b<3>(cap));
+    MK_CUDA(set_smem_b<4>(cap));
+    g_static_ptr[device] = ptr;
+  }
+  *out = g_static_ptr[device];
+  return MK_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int mk_init(const MkConfig* cfg, int device, MkModel** out) {
@@ -359,6 +404,96 @@ int mk_load_weights(MkModel* m, const MkWeights* w) {
 int mk_decode(MkModel* m, const int32_t* tokens, const int32_t* positions, int32_t batch,
               const MkKVCache* kv, float* logits, int32_t* next_ids, int32_t flags, void* stream) {
   return enqueue(m, 0, tokens, positions, batch, kv, nullptr, nullptr, logits, next_ids, flags,
+                 stream);
+}
+
+int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tokens,
+                     const int32_t* positions, int32_t batch, const MkKVCache* kv, float* logits,
+                     int32_t* next_ids, int32_t flags, int32_t* error_out, void* stream) {
+  int rc = validate_config(cfg);
+  if (rc) return rc;
+  if (!w) return fail(MK_EINVAL, "weights are NULL");
+  int device = 0;
+  MK_CUDA(cudaGetDevice(&device));
+  int major = 0, coop = 0, sms = 0, cap = 0;
+  MK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+  MK_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+  MK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  MK_CUDA(cudaDeviceGetAttribute(&cap, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  if (major != 10) return fail(MK_EINVAL, "device %d is not sm_100a", device);
+  if (!coop) return fail(MK_EINVAL, "device lacks cooperative launch");
+
+  // The launch plan, computed like mk_init's, in a handle on the stack.
+  MkModel m;
+  m.cfg = *cfg;
+  m.device = device;
+  m.num_sms = sms;
+  m.grid = sms;
+  m.kmax = std::max(std::max(cfg->hidden, cfg->intermediate), cfg->num_q_heads * 64);
+  const int B = cfg->max_batch;
+  {
+    auto per_cta = [sms](int units) { return (units + sms - 1) / sms; };
+    const int nh = mk::pieces_per_row(cfg->hidden), nqd = mk::pieces_per_row(cfg->num_q_heads * 64),
+              ni = mk::pieces_per_row(cfg->intermediate);
+    int pc = per_cta((cfg->num_q_heads + 2 * cfg->num_kv_heads) * 32) * 2 * nh;
+    pc = std::max(pc, per_cta(cfg->hidden) * nqd);
+    pc = std::max(pc, per_cta(cfg->intermediate) * 2 * nh);
+    pc = std::max(pc, per_cta(cfg->hidden) * ni);
+    m.part_cap = pc * B;
+  }
+  for (int s = 16; s >= 4 && !m.num_slots; --s)
+    if (mk::smem_bytes_for(s, B, m.kmax, m.part_cap, cfg->hidden) <= cap) m.num_slots = s;
+  if (!m.num_slots) return fail(MK_EINVAL, "activation rows (%d x %d) leave no room for the ring", B, m.kmax);
+  m.smem = mk::smem_bytes_for(m.num_slots, B, m.kmax, m.part_cap, cfg->hidden);
+
+  // Scratch layout (as mk_init's), checked against the static array's size.
+  const size_t H = cfg->hidden, I = cfg->intermediate, NQ = cfg->num_q_heads,
+               NKV = cfg->num_kv_heads;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t o_h = take(B * H * 2);
+  const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 2);
+  const size_t o_attn = take(B * NQ * 64 * 2);
+  const size_t o_act = take(B * I * 2);
+  const size_t o_part = take(B * NKV * mk::kMaxSplit * mk::kGroup * mk::kPartialStride * 4);
+  const size_t o_cnt = take((mk::kCntArrive + B * NKV) * 4);
+  const size_t o_keys = take(B * 8);
+  const size_t o_err = take(16);
+  const size_t o_mirror = take(16);
+  if (off > kStaticScratchBytes)
+    return fail(MK_EINVAL,
+                "mk_decode_static: this geometry needs %zu bytes of scratch, the static array "
+                "holds %zu (use mk_init / mk_decode instead)",
+                off, kStaticScratchBytes);
+
+  void* base = nullptr;
+  rc = static_setup(device, &base);
+  if (rc) return rc;
+  char* cb = static_cast<char*>(base);
+  m.h = reinterpret_cast<mk::bf16*>(cb + o_h);
+  m.qkv = reinterpret_cast<mk::bf16*>(cb + o_qkv);
+  m.attn = reinterpret_cast<mk::bf16*>(cb + o_attn);
+  m.act = reinterpret_cast<mk::bf16*>(cb + o_act);
+  m.partials = reinterpret_cast<float*>(cb + o_part);
+  m.counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
+  m.keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
+  m.error = reinterpret_cast<int*>(cb + o_err);
+  // Device-side failures are reported in error_out (or a slot of the static
+  // array when the caller passes none) instead of a mapped host mirror.
+  m.host_error_dev = error_out ? reinterpret_cast<int*>(error_out) : reinterpret_cast<int*>(cb + o_mirror);
+  rc = mk_load_weights(&m, w);
+  if (rc) return rc;
+
+  // What must start at zero: barrier and arrival counters, argmax keys and
+  // error words (a previous call that failed on the device leaves them set).
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  MK_CUDA(cudaMemsetAsync(cb + o_cnt, 0, o_mirror + 16 - o_cnt, st));
+  if (error_out) MK_CUDA(cudaMemsetAsync(error_out, 0, 4 * sizeof(int32_t), st));
+  return enqueue(&m, 0, tokens, positions, batch, kv, nullptr, nullptr, logits, next_ids, flags,
                  stream);
 }
 
