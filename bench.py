@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a few steps, no e2e / sweep / cpu baseline")
+    ap.add_argument("--case", choices=["small4"], default=None,
+                    help="small4: ncu profiling case - 4 Llama-3.2-1B layers, vocab 32000, one "
+                         "step at ctx 512 after 4 warm-up steps (prints its time, no JSON line)")
     return ap.parse_args()
 
 
@@ -410,8 +413,41 @@ def run_ours(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_case_small4():
+    """The ncu case: Llama-3.2-1B-shaped layers, small enough to replay (~0.7 GB)."""
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B
+    from llama1b_megakernel_b200.model import MegakernelLlamaForCausalLM
+
+    cfg = LLAMA_3_2_1B.replace(num_layers=4, vocab=32000)
+    dev = torch.device("cuda", 0)
+    w = syn.make_weights(cfg, seed=0, device=dev)
+    m = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=1024, page_size=64, device=dev)
+    del w
+    k, v = syn.random_kv_rows(cfg, 512, seed=5, device=dev)
+    m.kv.fill(0, k, v)
+    m.kv.reserve(0, 1024)
+    del k, v
+    tok = torch.tensor([7], dtype=torch.int32, device=dev)
+    pos = torch.tensor([512], dtype=torch.int32, device=dev)
+    nxt = torch.empty(1, dtype=torch.int32, device=dev)
+    for _ in range(4):
+        m.launch(tok, pos, m.kv, None, nxt)
+    m.sync()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    m.launch(tok, pos, m.kv, None, nxt)
+    ev[1].record()
+    torch.cuda.synchronize()
+    m.sync()
+    print(f"small4 step {ev[0].elapsed_time(ev[1]):.4f} ms")
+
+
 def main():
     args = parse()
+    if args.case == "small4":
+        run_case_small4()
+        return
     ws, rank, local = dist_init()
     try:
         if args.impl == "reference":

@@ -26,9 +26,12 @@ constexpr int kProducers = 2;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + kProducers * 32;
 constexpr int kSegCols = 2048;             // max columns of one piece (a row segment)
-constexpr int kAttnChunk = 64;             // cached positions per attention slot
+// Cached positions per attention slot: four per consumer warp, so every warp
+// takes one round of a full chunk (K rows in the slot's first 8 KB, V in its second).
+constexpr int kAttnChunk = 4 * kConsumerWarps;
+static_assert(kAttnChunk * kHeadDim * 2 <= kSlotBytes / 2, "a chunk's K rows must fit half a slot");
 constexpr int kMaxSplit = 32;              // split-K pieces per (sequence, kv head)
-constexpr int kSplitMinPositions = 512;    // no split shorter than this (8 chunks)
+constexpr int kSplitMinPositions = 512;    // no split shorter than this (~9 chunks)
 constexpr int kPartialStride = kHeadDim + 2;  // o[64], m, l per q head
 
 // Device error codes (error word [0]).

@@ -721,8 +721,8 @@ __device__ __forceinline__ void softmax_merge(float& m, float& l, float (&o)[8],
   m = M;
 }
 
-// Split-K GQA flash-decode for the CTA's items. A 64-position chunk is spread
-// over the consumer warps, four positions at a time: lane (h, j) of a warp
+// Split-K GQA flash-decode for the CTA's items. A chunk of kAttnChunk
+// positions is spread over the consumer warps, four each: lane (h, j) of a warp
 // scores position 4w + j/2 against q head h over half of the head dims (the
 // other half on lane j^1), with q kept in registers as packed bf16, then
 // accumulates dims [8j, 8j + 8) of P.V. Warp states are merged in shared
