@@ -174,9 +174,10 @@ int mk_sync(MkModel* m, void* stream);
 int mk_set_timeout_ns(MkModel* m, uint64_t ns);
 
 /*
- * Test knob for failure detection: CTA `cta` skips its arrival at the first
- * grid barrier of the next launches (-1 disables), so every other CTA's wait
- * runs out and the launch ends with MK_ETIMEOUT instead of hanging.
+ * Test knob for failure detection: CTA `cta` withholds its layer-0 q/k/v rows
+ * in the next launches (-1 disables), so the attention reads that wait for
+ * them run out of time and the launch ends with MK_ETIMEOUT instead of
+ * hanging.
  */
 int mk_debug_skip_arrival(MkModel* m, int32_t cta);
 

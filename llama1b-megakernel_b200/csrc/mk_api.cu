@@ -3,7 +3,7 @@
 // The handle owns the inter-phase scratch (residual, q/k/v, attention
 // partials, barrier counters, argmax keys, the device error word); everything
 // else is borrowed from the caller per call. Launches are cooperative so all
-// CTAs (one per SM) are co-resident, which the kernel's grid barriers need.
+// CTAs (one per SM) are co-resident, which the kernel's cross-CTA waits need.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -56,10 +56,11 @@ struct MkModel {
   int debug_skip_cta = -1;
   // scratch
   void* scratch = nullptr;
-  mk::bf16* h = nullptr;
-  mk::bf16* qkv = nullptr;
-  mk::bf16* attn = nullptr;
-  mk::bf16* act = nullptr;
+  uint32_t* h = nullptr;     // tagged activation words (see mk_kernel.cuh)
+  uint32_t* qkv = nullptr;
+  uint32_t* attn = nullptr;
+  uint32_t* act = nullptr;
+  uint32_t launch_seq = 0;   // launches so far: gives each launch its own tags
   float* partials = nullptr;
   uint32_t* counters = nullptr;
   unsigned long long* keys = nullptr;
@@ -212,6 +213,9 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   p.host_error = m->host_error_dev;
   p.timeout_ns = m->timeout_ns;
   p.debug_skip_cta = m->debug_skip_cta;
+  // 5 tagged phases per layer plus the lm_head; tags stay distinct across
+  // the 65535 / (5 L + 1) launches before they repeat.
+  p.tag_base = (uint32_t)(((uint64_t)m->launch_seq++ * (uint64_t)(5 * c.num_layers + 1)) % 65535u);
   p.trace = m->trace;
   p.trace_per_cta = (c.num_layers * 5 + 1) * mk::kTraceKinds;
   MK_CUDA(dispatch_launch(batch, p, m->grid, m->smem, static_cast<cudaStream_t>(stream)));
@@ -236,6 +240,7 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_ptr[kStaticMaxDevices] = {};  // device address of g_static_scratch, per device
+uint32_t g_static_seq[kStaticMaxDevices] = {};  // launches so far per device (tags, see enqueue)
 
 // Once per device, with that device current: the array's device address (the
 // host-side name g_static_scratch is only a stand-in and must never reach a
@@ -344,10 +349,10 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
     off += (bytes + 255) & ~size_t(255);
     return o;
   };
-  const size_t o_h = take(B * H * 2);
-  const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 2);
-  const size_t o_attn = take(B * NQ * 64 * 2);
-  const size_t o_act = take(B * I * 2);
+  const size_t o_h = take(B * H * 4);
+  const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 4);
+  const size_t o_attn = take(B * NQ * 64 * 4);
+  const size_t o_act = take(B * I * 4);
   const size_t o_part = take(B * NKV * mk::kMaxSplit * mk::kGroup * mk::kPartialStride * 4);
   const size_t o_cnt = take((mk::kCntArrive + B * NKV) * 4);
   const size_t o_keys = take(B * 8);
@@ -361,10 +366,10 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   }
   m->scratch = base;
   char* cb = static_cast<char*>(base);
-  m->h = reinterpret_cast<mk::bf16*>(cb + o_h);
-  m->qkv = reinterpret_cast<mk::bf16*>(cb + o_qkv);
-  m->attn = reinterpret_cast<mk::bf16*>(cb + o_attn);
-  m->act = reinterpret_cast<mk::bf16*>(cb + o_act);
+  m->h = reinterpret_cast<uint32_t*>(cb + o_h);
+  m->qkv = reinterpret_cast<uint32_t*>(cb + o_qkv);
+  m->attn = reinterpret_cast<uint32_t*>(cb + o_attn);
+  m->act = reinterpret_cast<uint32_t*>(cb + o_act);
   m->partials = reinterpret_cast<float*>(cb + o_part);
   m->counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
   m->keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
@@ -455,10 +460,10 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
     off += (bytes + 255) & ~size_t(255);
     return o;
   };
-  const size_t o_h = take(B * H * 2);
-  const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 2);
-  const size_t o_attn = take(B * NQ * 64 * 2);
-  const size_t o_act = take(B * I * 2);
+  const size_t o_h = take(B * H * 4);
+  const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 4);
+  const size_t o_attn = take(B * NQ * 64 * 4);
+  const size_t o_act = take(B * I * 4);
   const size_t o_part = take(B * NKV * mk::kMaxSplit * mk::kGroup * mk::kPartialStride * 4);
   const size_t o_cnt = take((mk::kCntArrive + B * NKV) * 4);
   const size_t o_keys = take(B * 8);
@@ -474,10 +479,10 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   rc = static_setup(device, &base);
   if (rc) return rc;
   char* cb = static_cast<char*>(base);
-  m.h = reinterpret_cast<mk::bf16*>(cb + o_h);
-  m.qkv = reinterpret_cast<mk::bf16*>(cb + o_qkv);
-  m.attn = reinterpret_cast<mk::bf16*>(cb + o_attn);
-  m.act = reinterpret_cast<mk::bf16*>(cb + o_act);
+  m.h = reinterpret_cast<uint32_t*>(cb + o_h);
+  m.qkv = reinterpret_cast<uint32_t*>(cb + o_qkv);
+  m.attn = reinterpret_cast<uint32_t*>(cb + o_attn);
+  m.act = reinterpret_cast<uint32_t*>(cb + o_act);
   m.partials = reinterpret_cast<float*>(cb + o_part);
   m.counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
   m.keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
@@ -487,6 +492,10 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   m.host_error_dev = error_out ? reinterpret_cast<int*>(error_out) : reinterpret_cast<int*>(cb + o_mirror);
   rc = mk_load_weights(&m, w);
   if (rc) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    m.launch_seq = g_static_seq[device]++;
+  }
 
   // What must start at zero: barrier and arrival counters, argmax keys and
   // error words (a previous call that failed on the device leaves them set).

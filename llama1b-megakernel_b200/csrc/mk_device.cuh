@@ -1,7 +1,7 @@
 // mk_device.cuh — device helpers for the decode megakernel (sm_100a).
 //
 // mbarrier + bulk-copy (TMA, non-tensor) primitives written as inline PTX,
-// acquire/release global atomics for the grid-wide phase barriers, bf16
+// acquire/release global atomics for the cross-CTA counters, bf16
 // conversion helpers and a time-bounded wait policy. Nothing here spins
 // without a limit: every wait checks the global timer and a shared abort word.
 #pragma once
@@ -46,10 +46,8 @@ enum DevErr : int {
 
 // Counters in the scratch counter block.
 enum Counter : int {
-  kCntBarrier = 0,
-  kCntHeadsDone = 1,
-  kCntDone = 2,
-  kCntArrive = 4,  // + b * nkv + g
+  kCntDone = 2,    // CTAs finished with the step (the last publishes the argmax)
+  kCntArrive = 4,  // + b * nkv + g: attention splits finished per (sequence, kv head)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

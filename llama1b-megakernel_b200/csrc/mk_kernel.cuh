@@ -87,11 +87,12 @@ struct Params {
   bf16* hidden_out;
   float* logits;
   int* next_ids;
-  // scratch (owned by the model handle)
-  bf16* h;         // [B][H]
-  bf16* qkv;       // [B][NQ + 2 NKV][64]
-  bf16* attn;      // [B][NQ * 64]
-  bf16* act;       // [B][I]
+  // scratch (owned by the model handle). Activations passed between phases
+  // are tagged words: bf16 bits << 16 | a 16-bit tag (see phase_tag).
+  uint32_t* h;     // [B][H]
+  uint32_t* qkv;   // [B][NQ + 2 NKV][64]
+  uint32_t* attn;  // [B][NQ * 64]
+  uint32_t* act;   // [B][I]
   float* partials; // [B][NKV][kMaxSplit][kGroup][kPartialStride]
   uint32_t* counters;
   unsigned long long* keys;  // [B]
@@ -99,6 +100,7 @@ struct Params {
   int* host_error;           // [4] mapped pinned host mirror of `error`
   unsigned long long timeout_ns;
   int debug_skip_cta;
+  uint32_t tag_base;  // this launch's first tag (consecutive launches use disjoint tags)
   // optional phase trace ([grid][trace_per_cta] u64, see kTrace*); nullptr = off
   unsigned long long* trace;
   int trace_per_cta;
@@ -177,6 +179,70 @@ __device__ __noinline__ void raise_error(const Params& p, int code, int where) {
 }
 
 __device__ __forceinline__ bool aborted(const Params& p) { return ld_volatile_i32(p.error) != 0; }
+
+// ---------------------------------------------------------------- tagged activations
+//
+// Every activation one phase hands to the next (q/k/v, attention output, the
+// residual h, the SwiGLU product) is written as 32-bit words, bf16 bits << 16
+// | a 16-bit tag naming the launch and the phase that wrote it. A reader polls
+// the words themselves until each carries the tag it expects, so there is no
+// grid barrier and no separate flag round trip between a phase and the next.
+// A single buffer per activation is safe: no phase can overwrite a word
+// before every CTA has read the previous value, because its own inputs depend
+// on all CTAs having done so. Tags are never 0, the value scratch starts at.
+
+__device__ __forceinline__ uint32_t phase_tag(const Params& p, int phase) {
+  return 1u + (p.tag_base + (uint32_t)phase) % 65535u;
+}
+
+__device__ __forceinline__ uint32_t tagged(float v, uint32_t tag) {
+  return ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)) << 16) | tag;
+}
+
+__device__ __forceinline__ bool tags_ok(const uint4& u, uint32_t tag) {
+  return ((u.x & 0xFFFFu) == tag) & ((u.y & 0xFFFFu) == tag) & ((u.z & 0xFFFFu) == tag) &
+         ((u.w & 0xFFFFu) == tag);
+}
+
+struct Polled {
+  uint4 u;
+  int ok;
+};
+
+// Slow path of poll_tagged: re-read until the tags match (time-bounded).
+// Returns by value so callers' registers stay out of local memory.
+__device__ __noinline__ Polled poll_tagged_slow(const Params& p, const uint32_t* src, uint32_t tag,
+                                                int where) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src));
+    if (tags_ok(u, tag)) return {u, 1};
+    if ((it & 15) == 0) {
+      if (aborted(p)) return {u, 0};
+      if (global_ns() - t0 > p.timeout_ns) {
+        raise_error(p, kErrBarrierTimeout, where);
+        return {u, 0};
+      }
+    }
+  }
+}
+
+// Four tagged words (16-byte aligned) once all carry `tag`. false on abort or
+// timeout (the thread's own verdict; callers make it CTA-wide).
+__device__ __forceinline__ bool poll_tagged(const Params& p, const uint32_t* src, uint32_t tag,
+                                            uint4& out, int where) {
+  out = __ldcg(reinterpret_cast<const uint4*>(src));
+  if (tags_ok(out, tag)) return true;
+  const Polled r = poll_tagged_slow(p, src, tag, where);
+  out = r.u;
+  return r.ok != 0;
+}
+
+// The bf16 values of four tagged words, packed two per word.
+__device__ __forceinline__ uint2 untag4(const uint4& u) {
+  return make_uint2((u.x >> 16) | (u.y & 0xFFFF0000u), (u.z >> 16) | (u.w & 0xFFFF0000u));
+}
 
 // Spin until *c >= target (wrap-safe). false on timeout or abort.
 __device__ __noinline__ bool counter_wait(const Params& p, const uint32_t* c, uint32_t target,
@@ -544,6 +610,106 @@ __device__ void load_rows(const bf16* const (&src)[B], int K, const bf16* gamma,
   consumer_sync();
 }
 
+// load_rows for tagged activations: poll B rows of K (<= 8192) tagged words
+// until they carry `tag`, store the bf16 values (and optionally a raw copy)
+// and apply the same RMSNorm. A thread issues all its loads, and its gamma
+// loads, before waiting on any, so a ready row costs one round trip. false =
+// abort, for every consumer thread.
+template <int B>
+struct RowPtrs {
+  const uint32_t* r[B];
+};
+
+template <int B>
+__device__ __noinline__ bool load_rows_tagged(const Params& p, RowPtrs<B> src, int K, uint32_t tag,
+                                              const bf16* gamma, float eps, bf16* xs, int kmax,
+                                              SmemState& st, int where, bf16* raw) {
+  constexpr int kBatch = 5;   // uint4 of tagged words per thread per row: 2048 / 448 -> 5
+  constexpr int kGBatch = 2;  // uint4 of gamma per thread: (hidden <= 4096) / 8 / 448 -> 2
+  const int tid = threadIdx.x;
+  const int k4 = K >> 2, k8 = K >> 3;
+  uint4 gv[kGBatch];
+  if (gamma) {
+#pragma unroll
+    for (int j = 0; j < kGBatch; ++j) {
+      const int v = tid + j * kConsumerThreads;
+      if (v < k8) gv[j] = __ldg(reinterpret_cast<const uint4*>(gamma) + v);
+    }
+  }
+  float ss[B];
+  int ok = 1;
+#pragma unroll
+  for (int b = 0; b < B; ++b) {
+    ss[b] = 0.f;
+    uint4 u[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int v = tid + i * kConsumerThreads;
+      if (v < k4) u[i] = __ldcg(reinterpret_cast<const uint4*>(src.r[b] + 4 * v));
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int v = tid + i * kConsumerThreads;
+      if (v < k4) {
+        if (!tags_ok(u[i], tag)) {
+          const Polled r = poll_tagged_slow(p, src.r[b] + 4 * v, tag, where);
+          u[i] = r.u;
+          ok &= r.ok;
+        }
+        const uint2 w = untag4(u[i]);
+        reinterpret_cast<uint2*>(xs + b * kmax)[v] = w;
+        if (raw) reinterpret_cast<uint2*>(raw + b * K)[v] = w;
+        const float a0 = bf_lo(w.x), a1 = bf_hi(w.x), a2 = bf_lo(w.y), a3 = bf_hi(w.y);
+        ss[b] += a0 * a0;
+        ss[b] += a1 * a1;
+        ss[b] += a2 * a2;
+        ss[b] += a3 * a3;
+      }
+    }
+  }
+  if (consumer_any(!ok)) return false;
+  if (gamma) {
+    const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const float t = warp_sum(ss[b]);
+      if (lane == 0) st.red[warp * B + b] = t;
+    }
+    consumer_sync();
+    float r[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) t += st.red[w * B + b];
+      const float var = __fdiv_rn(t, (float)K);
+      r[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    }
+#pragma unroll
+    for (int j = 0; j < kGBatch; ++j) {
+      const int v = tid + j * kConsumerThreads;
+      if (v >= k8) continue;
+      const uint32_t gw[4] = {gv[j].x, gv[j].y, gv[j].z, gv[j].w};
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        uint4* px = reinterpret_cast<uint4*>(xs + b * kmax) + v;
+        uint4 u = *px;
+        uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = rbf(rbf(bf_lo(w[e]) * r[b]) * bf_lo(gw[e]));
+          const float hi = rbf(rbf(bf_hi(w[e]) * r[b]) * bf_hi(gw[e]));
+          __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+          w[e] = *reinterpret_cast<uint32_t*>(&pr);
+        }
+        *px = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+  consumer_sync();
+  return true;
+}
+
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   f[0] = bf_lo(u.x); f[1] = bf_hi(u.x);
   f[2] = bf_lo(u.y); f[3] = bf_hi(u.y);
@@ -644,24 +810,6 @@ __device__ __noinline__ bool gemv_phase(const Params& p, Ring& ring_io, uint32_t
   return true;
 }
 
-// End of a phase: agree across the consumer warps whether every warp
-// finished it (`ok`), then arrive at the grid barrier. false = abort (all
-// consumer threads see the same answer).
-__device__ __forceinline__ bool grid_arrive(const Params& p, bool ok, bool skip) {
-  if (consumer_any(!ok)) return false;
-  // The release add is cumulative: the CTA's writes, ordered before it by
-  // the named barrier above, are visible to any CTA that acquires the count.
-  if (threadIdx.x == 0 && !skip) red_release_add_u32(p.counters + kCntBarrier, 1u);
-  return true;
-}
-
-// Wait until *counter >= target: thread 0 spins (time-bounded), the other
-// consumer threads park on the named barrier. false = abort, for everyone.
-__device__ __forceinline__ bool grid_wait(const Params& p, uint32_t* counter, uint32_t target,
-                                          int where) {
-  const bool ok = (threadIdx.x == 0) ? counter_wait(p, counter, target, where) : true;
-  return !consumer_any(!ok);
-}
 
 static_assert(kConsumerThreads >= kGroup * kHeadDim + kGroup * kMaxSplit,
               "merge_group needs a thread per (head, dim) plus one per (head, split)");
@@ -672,7 +820,8 @@ static_assert(kGroup * kMaxSplit * 2 <= kAttnWarps * kGroup * kPartialStride,
 // (m, l, o) — split 0 already holds the new token's own K/V — and writes the
 // group's bf16 head outputs. All consumer threads call it. The per-split
 // loads are issued before any is used, so the merge costs one L2 round trip.
-__device__ __noinline__ void merge_group(const Params& p, int b, int g, int ns, float* ml) {
+__device__ __noinline__ void merge_group(const Params& p, int b, int g, int ns, float* ml,
+                                         uint32_t tag) {
   const int tid = threadIdx.x;
   const float* base = p.partials + ((size_t)b * p.NKV + g) * kMaxSplit * kGroup * kPartialStride;
   const bool worker = tid < kGroup * kHeadDim;
@@ -704,7 +853,7 @@ __device__ __noinline__ void merge_group(const Params& p, int b, int g, int ns, 
         O += f * os[s];
       }
     }
-    p.attn[(size_t)b * p.NQ * kHeadDim + (g * kGroup + hh) * kHeadDim + d] = f2bf(O / L);
+    p.attn[(size_t)b * p.NQ * kHeadDim + (g * kGroup + hh) * kHeadDim + d] = tagged(O / L, tag);
   }
 }
 
@@ -744,22 +893,32 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
   for (int it = blockIdx.x; it < T; it += gridDim.x) {
     const AttnItem a = attn_item(p, st, it);
     consumer_sync();
-    // q of the group's heads, and the new token's own K and V row, in one
-    // round trip.
-    if (tid < kGroup * kHeadDim / 8) {
-      reinterpret_cast<uint4*>(qs)[tid] =
-          __ldcg(reinterpret_cast<const uint4*>(p.qkv + ((size_t)a.b * NQKV + a.g * kGroup) * kHeadDim) + tid);
-    } else if (tid < kGroup * kHeadDim / 8 + 16) {
-      const int r = tid - kGroup * kHeadDim / 8;  // 0..7 K, 8..15 V
-      const int head = (r < 8) ? p.NQ + a.g : p.NQ + p.NKV + a.g;
-      const uint4 u =
-          __ldcg(reinterpret_cast<const uint4*>(p.qkv + ((size_t)a.b * NQKV + head) * kHeadDim) + (r & 7));
-      float f[8];
-      unpack8(u, f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) kvn[(r >> 3) * kHeadDim + (r & 7) * 8 + e] = f[e];
+    // q of the group's heads, and the new token's own K and V row, polled
+    // until the QKV phase's tag is on them (one round trip when ready).
+    bool qfail = false;
+    {
+      const uint32_t tag = phase_tag(p, layer * 5 + 0);
+      constexpr int kQ4 = kGroup * kHeadDim / 4;  // q words in uint4s
+      if (tid < kQ4 + 2 * kHeadDim / 4) {
+        const bool is_q = tid < kQ4;
+        const int r = is_q ? tid : tid - kQ4;  // uint4 index within q, or within K|V
+        const int head = is_q ? a.g * kGroup : (r < kHeadDim / 4 ? p.NQ + a.g : p.NQ + p.NKV + a.g);
+        const int off = is_q ? r * 4 : (r % (kHeadDim / 4)) * 4;
+        uint4 u;
+        if (!poll_tagged(p, p.qkv + ((size_t)a.b * NQKV + head) * kHeadDim + off, tag, u, 3000 + layer)) {
+          qfail = true;
+        } else if (is_q) {
+          reinterpret_cast<uint2*>(qs)[r] = untag4(u);
+        } else {
+          float* dst = kvn + (r / (kHeadDim / 4)) * kHeadDim + off;
+          dst[0] = __uint_as_float(u.x & 0xFFFF0000u);
+          dst[1] = __uint_as_float(u.y & 0xFFFF0000u);
+          dst[2] = __uint_as_float(u.z & 0xFFFF0000u);
+          dst[3] = __uint_as_float(u.w & 0xFFFF0000u);
+        }
+      }
     }
-    consumer_sync();
+    if (consumer_any(qfail)) return false;
     if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnQ, global_ns());
     uint4 qh[4];
 #pragma unroll
@@ -894,7 +1053,8 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
       }
       if (ns == 1) {
         // The only split (it holds the active slot, so L > 0): final output.
-        p.attn[(size_t)a.b * p.NQ * kHeadDim + (a.g * kGroup + hh) * kHeadDim + d] = f2bf(O / L);
+        p.attn[(size_t)a.b * p.NQ * kHeadDim + (a.g * kGroup + hh) * kHeadDim + d] =
+            tagged(O / L, phase_tag(p, layer * 5 + 1));
       } else {
         float* pp2 = p.partials +
                      ((((size_t)a.b * p.NKV + a.g) * kMaxSplit + a.s) * kGroup + hh) * kPartialStride;
@@ -905,14 +1065,12 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
         }
       }
     }
-    consumer_sync();
     if (ns == 1) {
-      if (tid == 0) {
-        red_release_add_u32(p.counters + kCntHeadsDone, 1u);
-        if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
-      }
+      // The tagged outputs are the publication.
+      if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
       continue;
     }
+    consumer_sync();
     // Count the split; the last one of its (seq, kv head) merges them all.
     if (tid == 0) {
       uint32_t* arr = p.counters + kCntArrive + a.b * p.NKV + a.g;
@@ -924,12 +1082,8 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
     }
     consumer_sync();
     if (st.flag) {
-      merge_group(p, a.b, a.g, ns, comb);
-      consumer_sync();
-      if (tid == 0) {
-        red_release_add_u32(p.counters + kCntHeadsDone, 1u);
-        if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnMerged, global_ns());
-      }
+      merge_group(p, a.b, a.g, ns, comb, phase_tag(p, layer * 5 + 1));
+      if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnMerged, global_ns());
     }
   }
   return true;
@@ -983,8 +1137,6 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
   const int H = p.H, I = p.I, QD = p.NQ * kHeadDim, NQKV = p.NQ + 2 * p.NKV;
   const uint32_t xs_s = smem_addr(xs);
   Sched sch;
-  uint32_t barriers = 0;  // grid barriers passed so far
-  const int G = gridDim.x;
   auto mark = [&](int ph, int kind) {
     if (p.trace && threadIdx.x == 0) trace_put(p, ph, kind, global_ns());
   };
@@ -1006,25 +1158,30 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
   for (int l = 0; l < p.L; ++l) {
     // ------------------------------------------------------------- QKV
     mark(l * 5 + 0, kTrWaitStart);
-    if (l > 0) {
-      if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 1000 + l)) return;
-    }
     mark(l * 5 + 0, kTrWaitDone);
-    {
+    if (l == 0) {
       const bf16* src[B];
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        src[b] = (l > 0) ? p.h + (size_t)b * H
-                 : (p.mode == 0 ? p.embed + (size_t)st.tok[b] * H : p.hidden_in + (size_t)b * H);
-      }
-      load_rows<B>(src, H, p.norm_attn + (size_t)l * H, p.eps, xs, p.kmax, st, raw);
+      for (int b = 0; b < B; ++b)
+        src[b] = p.mode == 0 ? p.embed + (size_t)st.tok[b] * H : p.hidden_in + (size_t)b * H;
+      load_rows<B>(src, H, p.norm_attn, p.eps, xs, p.kmax, st, raw);
+    } else {
+      RowPtrs<B> src;
+#pragma unroll
+      for (int b = 0; b < B; ++b) src.r[b] = p.h + (size_t)b * H;
+      if (!load_rows_tagged<B>(p, src, H, phase_tag(p, (l - 1) * 5 + 4), p.norm_attn + (size_t)l * H,
+                               p.eps, xs, p.kmax, st, 1000 + l, raw))
+        return;
     }
     mark(l * 5 + 0, kTrRowsLoaded);
     const Split sq = sch.next(NQKV * 32);
     bool ok = gemv_phase<B>(p, ring, xs_s, H, p.nseg_h, 2, 1, sq, 2000 + l, to_part);
     if (consumer_any(!ok)) return;
-    {
+    // The failure-detection knob: one CTA withholds its layer-0 q/k/v rows,
+    // so the attention reads that poll for them run out of time.
+    if (!(l == 0 && (int)blockIdx.x == p.debug_skip_cta)) {
       const size_t kv_layer = (size_t)l * p.num_pages * p.NKV * p.page_size * kHeadDim;
+      const uint32_t tag = phase_tag(p, l * 5 + 0);
       const int nu = sq.u1 - sq.u0, ns = p.nseg_h;
       for (int i = tid; i < nu * B; i += kConsumerThreads) {
         const int ul = i / B, b = i % B, u = sq.u0 + ul;
@@ -1042,9 +1199,9 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
           x0 = y0;
           x1 = y1;
         }
-        bf16* qrow = p.qkv + ((size_t)b * NQKV + hh) * kHeadDim;
-        qrow[d] = f2bf(x0);
-        qrow[d + 32] = f2bf(x1);
+        uint32_t* qrow = p.qkv + ((size_t)b * NQKV + hh) * kHeadDim;
+        qrow[d] = tagged(x0, tag);
+        qrow[d + 32] = tagged(x1, tag);
         if (hh >= p.NQ) {
           const bool is_k = hh < p.NQ + p.NKV;
           const int g = is_k ? hh - p.NQ : hh - p.NQ - p.NKV;
@@ -1061,26 +1218,23 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       }
     }
     mark_done(l * 5 + 0);
-    if (!grid_arrive(p, ok, l == 0 && (int)blockIdx.x == p.debug_skip_cta)) return;
-    ++barriers;
 
     // ------------------------------------------------------------- ATTN
     mark(l * 5 + 1, kTrWaitStart);
-    if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 3000 + l)) return;
     mark(l * 5 + 1, kTrWaitDone);
     if (!attention_phase<B>(p, ring, st, l, comb, qs, kvn)) return;
     mark_done(l * 5 + 1);
 
     // ------------------------------------------------------------- O
     mark(l * 5 + 2, kTrWaitStart);
-    if (!grid_wait(p, p.counters + kCntHeadsDone, (uint32_t)((l + 1) * B * p.NKV), 4000 + l))
-      return;
     mark(l * 5 + 2, kTrWaitDone);
     {
-      const bf16* src[B];
+      RowPtrs<B> src;
 #pragma unroll
-      for (int b = 0; b < B; ++b) src[b] = p.attn + (size_t)b * QD;
-      load_rows<B>(src, QD, nullptr, 0.f, xs, p.kmax, st);
+      for (int b = 0; b < B; ++b) src.r[b] = p.attn + (size_t)b * QD;
+      if (!load_rows_tagged<B>(p, src, QD, phase_tag(p, l * 5 + 1), nullptr, 0.f, xs, p.kmax, st,
+                               4000 + l, nullptr))
+        return;
     }
     mark(l * 5 + 2, kTrRowsLoaded);
     {
@@ -1092,22 +1246,21 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         const int ul = i / B, b = i % B, u = so.u0 + ul;
         // residual: the layer input, kept raw by the QKV phase's row load
         const float r = bf2f(raw[b * H + u]);
-        p.h[(size_t)b * H + u] = f2bf(r + rbf(row_sum(ul * ns, ns, b)));
+        p.h[(size_t)b * H + u] = tagged(r + rbf(row_sum(ul * ns, ns, b)), phase_tag(p, l * 5 + 2));
       }
     }
     mark_done(l * 5 + 2);
-    if (!grid_arrive(p, ok, false)) return;
-    ++barriers;
 
     // ------------------------------------------------------------- GU
     mark(l * 5 + 3, kTrWaitStart);
-    if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 6000 + l)) return;
     mark(l * 5 + 3, kTrWaitDone);
     {
-      const bf16* src[B];
+      RowPtrs<B> src;
 #pragma unroll
-      for (int b = 0; b < B; ++b) src[b] = p.h + (size_t)b * H;
-      load_rows<B>(src, H, p.norm_mlp + (size_t)l * H, p.eps, xs, p.kmax, st, raw);
+      for (int b = 0; b < B; ++b) src.r[b] = p.h + (size_t)b * H;
+      if (!load_rows_tagged<B>(p, src, H, phase_tag(p, l * 5 + 2), p.norm_mlp + (size_t)l * H, p.eps,
+                               xs, p.kmax, st, 6000 + l, raw))
+        return;
     }
     mark(l * 5 + 3, kTrRowsLoaded);
     {
@@ -1120,22 +1273,21 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         const float g = rbf(row_sum(ul * 2 * ns, ns, b));
         const float up = rbf(row_sum(ul * 2 * ns + ns, ns, b));
         const float s = rbf(__fdiv_rn(g, 1.0f + expf(-g)));
-        p.act[(size_t)b * I + u] = f2bf(s * up);
+        p.act[(size_t)b * I + u] = tagged(s * up, phase_tag(p, l * 5 + 3));
       }
     }
     mark_done(l * 5 + 3);
-    if (!grid_arrive(p, ok, false)) return;
-    ++barriers;
 
     // ------------------------------------------------------------- DOWN
     mark(l * 5 + 4, kTrWaitStart);
-    if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 8000 + l)) return;
     mark(l * 5 + 4, kTrWaitDone);
     {
-      const bf16* src[B];
+      RowPtrs<B> src;
 #pragma unroll
-      for (int b = 0; b < B; ++b) src[b] = p.act + (size_t)b * I;
-      load_rows<B>(src, I, nullptr, 0.f, xs, p.kmax, st);
+      for (int b = 0; b < B; ++b) src.r[b] = p.act + (size_t)b * I;
+      if (!load_rows_tagged<B>(p, src, I, phase_tag(p, l * 5 + 3), nullptr, 0.f, xs, p.kmax, st,
+                               8000 + l, nullptr))
+        return;
     }
     mark(l * 5 + 4, kTrRowsLoaded);
     const bool last_layer = (l == p.L - 1);
@@ -1148,30 +1300,25 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         const int ul = i / B, b = i % B, u = sd.u0 + ul;
         // residual: h after o_proj, kept raw by the GU phase's row load
         const float r = bf2f(raw[b * H + u]);
-        const bf16 y = f2bf(r + rbf(row_sum(ul * ns, ns, b)));
-        p.h[(size_t)b * H + u] = y;
-        if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = y;
+        const float y = r + rbf(row_sum(ul * ns, ns, b));
+        p.h[(size_t)b * H + u] = tagged(y, phase_tag(p, l * 5 + 4));
+        if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = f2bf(y);
       }
     }
     mark_done(l * 5 + 4);
-    if (last_layer && p.mode == 1) {
-      consumer_sync();
-    } else {
-      if (!grid_arrive(p, ok, false)) return;
-      ++barriers;
-    }
   }
 
   // --------------------------------------------------------------- LM head
   if (p.mode == 0) {
     mark(p.L * 5, kTrWaitStart);
-    if (!grid_wait(p, p.counters + kCntBarrier, barriers * G, 10000)) return;
     mark(p.L * 5, kTrWaitDone);
     {
-      const bf16* src[B];
+      RowPtrs<B> src;
 #pragma unroll
-      for (int b = 0; b < B; ++b) src[b] = p.h + (size_t)b * H;
-      load_rows<B>(src, H, p.norm_final, p.eps, xs, p.kmax, st);
+      for (int b = 0; b < B; ++b) src.r[b] = p.h + (size_t)b * H;
+      if (!load_rows_tagged<B>(p, src, H, phase_tag(p, (p.L - 1) * 5 + 4), p.norm_final, p.eps, xs,
+                               p.kmax, st, 10000, nullptr))
+        return;
     }
     mark(p.L * 5, kTrRowsLoaded);
     const Split sl = sch.next(p.V);
@@ -1217,7 +1364,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
   consumer_sync();
   if (tid == 0) {
     const uint32_t t = atom_add_acq_rel_u32(p.counters + kCntDone, 1u);
-    if (t == (uint32_t)G - 1) {
+    if (t == gridDim.x - 1) {
       if (p.mode == 0) {
         for (int b = 0; b < B; ++b) {
           const unsigned long long key = atomicExch(p.keys + b, 0ull);
@@ -1229,8 +1376,6 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
           }
         }
       }
-      atomicExch(p.counters + kCntBarrier, 0u);
-      atomicExch(p.counters + kCntHeadsDone, 0u);
       atomicExch(p.counters + kCntDone, 0u);
       __threadfence();
     }
