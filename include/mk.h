@@ -202,6 +202,14 @@ int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed
 /* Launch geometry chosen by mk_init: CTAs (one per SM) and ring slots per CTA. */
 int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem_bytes);
 
+/* The largest number of ring fills a consumer warp goes between two waits in
+ * the kernel's schedule for this geometry, batch and grid (-1 if a warp's
+ * first wait comes at fill 64 or later). mk_init refuses a geometry whose gap
+ * exceeds 64 - ring_slots - 8: the ring's 64 full barriers are told apart by
+ * parity, which is safe only within that distance. Host-only; no counterpart
+ * in the reference (its kernel has no software ring). */
+int mk_schedule_gap(const MkConfig* cfg, int32_t batch, int32_t grid, int32_t* gap);
+
 /* Last error message of the calling thread ("" if none). */
 const char* mk_last_error(void);
 

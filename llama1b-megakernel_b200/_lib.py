@@ -24,7 +24,7 @@ STATUS_NAMES = {
 EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
-    "mk_query", "mk_last_error", "mk_destroy",
+    "mk_query", "mk_schedule_gap", "mk_last_error", "mk_destroy",
 )
 
 
@@ -84,6 +84,7 @@ def load() -> ctypes.CDLL:
     lib.mk_debug_skip_arrival.argtypes = [VP, I32]
     lib.mk_set_trace.argtypes = [VP, VP, ctypes.c_int64, P(ctypes.c_int64)]
     lib.mk_query.argtypes = [VP, P(I32), P(I32), P(I32)]
+    lib.mk_schedule_gap.argtypes = [P(MkConfig), I32, I32, P(I32)]
     lib.mk_last_error.argtypes = []
     lib.mk_last_error.restype = ctypes.c_char_p
     lib.mk_destroy.argtypes = [VP]

@@ -98,3 +98,7 @@ SMALL = LlamaDecodeConfig(
     num_layers=3, hidden=512, intermediate=1536, num_q_heads=8, num_kv_heads=2,
     vocab=5003,
 )
+
+# Two Llama-3.2-1B-shaped layers with a small vocabulary: the full-size layer
+# geometry (a whole 16 KB down row per fill) at a size the oracle runs in seconds.
+MID = LlamaDecodeConfig(num_layers=2, vocab=4099)

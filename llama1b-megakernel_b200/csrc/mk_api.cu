@@ -7,11 +7,14 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/mk.h"
 #include "mk_kernel.cuh"
@@ -78,6 +81,82 @@ int64_t trace_entries(const MkModel* m) {
 }  // namespace
 
 namespace {
+
+// The consumer warps' ring waits are safe while a warp never goes more than
+// kFullBars - S - kProducerSlack fills between two waits, and its first wait
+// is on a fill below kFullBars (see the Ring comment in mk_kernel.cuh). This
+// walks every CTA's fill schedule as the kernel does (walk_schedule and
+// gemv_phase's item -> warp map) and returns the largest such gap. Attention
+// chunks are read by every warp except the last, partial chunk of an item, so
+// each attention item of the CTA counts as one fill no warp reads; the item
+// count is its maximum over positions.
+int max_consumer_gap(const MkConfig* c, int B, int G) {
+  constexpr int NC = mk::kConsumerWarps;
+  const int H = c->hidden, I = c->intermediate, QD = c->num_q_heads * 64;
+  const int NQKV = c->num_q_heads + 2 * c->num_kv_heads;
+  const int nh = mk::pieces_per_row(H), nqd = mk::pieces_per_row(QD), ni = mk::pieces_per_row(I);
+  const int ns = std::min(mk::kMaxSplit, std::max(1, G / (B * c->num_kv_heads)));
+  const int T = B * c->num_kv_heads * ns;
+  int worst = 0;
+  for (int cta = 0; cta < G; ++cta) {
+    int rot = 0;
+    long long f = 0;
+    long long last[NC];
+    for (int w = 0; w < NC; ++w) last[w] = -1;
+    auto gemv = [&](int U, int unit_bytes, int ipu) {
+      const mk::Split sp = mk::split_units(U, G, cta, rot);
+      rot = (rot + U % G) % G;
+      const int ups = mk::units_per_slot(unit_bytes);
+      for (int u = sp.u0; u < sp.u1; u += ups, ++f) {
+        const int P = std::min(ups, sp.u1 - u) * ipu, t0 = (u - sp.u0) * ipu;
+        for (int w = 0; w < NC; ++w) {
+          if (t0 + (w - t0 % NC + NC) % NC >= t0 + P) continue;  // no item for warp w
+          if (f >= mk::kFullBars)
+            worst = std::max(worst, last[w] < 0 ? INT32_MAX : (int)std::min<long long>(f - last[w], INT32_MAX));
+          last[w] = f;
+        }
+      }
+    };
+    const int items = cta < T ? (T - 1 - cta) / G + 1 : 0;
+    for (int l = 0; l < c->num_layers; ++l) {
+      gemv(NQKV * 32, 4 * H, 2 * nh);
+      f += items;
+      gemv(H, 2 * QD, nqd);
+      gemv(I, 4 * H, 2 * nh);
+      gemv(H, 2 * I, ni);
+    }
+    gemv(c->vocab, 2 * H, 1);
+  }
+  return worst;
+}
+
+// Every batch a launch may use (1 .. max_batch) has its own schedule.
+int check_schedule(const MkConfig* c, int max_batch, int G, int S) {
+  const int bound = mk::kFullBars - S - mk::kProducerSlack;
+  for (int B = 1; B <= max_batch; ++B) {
+    const int gap = max_consumer_gap(c, B, G);
+    if (gap > bound)
+      return fail(MK_EINVAL, "fill schedule at batch %d: a consumer warp would go %d fills between "
+                  "ring waits (at most %d are safe with %d slots)", B,
+                  gap == INT32_MAX ? -1 : gap, bound, S);
+  }
+  return MK_OK;
+}
+
+// check_schedule for the allocation-free entry point, which sets up on every
+// call: geometries already checked are remembered.
+int check_schedule_cached(const MkConfig* c, int B, int G, int S) {
+  static std::mutex mu;
+  static std::vector<std::array<int, 9>> ok;
+  const std::array<int, 9> key = {c->num_layers, c->hidden, c->intermediate, c->num_q_heads,
+                                  c->num_kv_heads, c->vocab, B, G, S};
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& k : ok)
+    if (k == key) return MK_OK;
+  const int rc = check_schedule(c, B, G, S);
+  if (rc == MK_OK) ok.push_back(key);
+  return rc;
+}
 
 int validate_config(const MkConfig* c) {
   if (!c) return fail(MK_EINVAL, "config is NULL");
@@ -304,8 +383,10 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
     cap = std::max(cap, per_cta(cfg->hidden) * ni);
     m->part_cap = cap * B;
   }
+  // An even slot count: producer k alone fills the slots s with s % 2 == k,
+  // so it sees every phase of their empty barriers.
   int slots = 0;
-  for (int s = 16; s >= 4; --s) {
+  for (int s = 16; s >= 4; s -= mk::kProducers) {
     if (mk::smem_bytes_for(s, B, m->kmax, m->part_cap, cfg->hidden) <= smem_cap) {
       slots = s;
       break;
@@ -317,6 +398,10 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   }
   m->num_slots = slots;
   m->smem = mk::smem_bytes_for(slots, B, m->kmax, m->part_cap, cfg->hidden);
+  if (int src = check_schedule(cfg, B, m->num_sms, slots)) {
+    delete m;
+    return src;
+  }
   // The attribute is per kernel, not per handle: allow the device maximum so
   // handles with different geometries can be used in any order.
   for (int b = 1; b <= 4; ++b) {
@@ -446,10 +531,11 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
     pc = std::max(pc, per_cta(cfg->hidden) * ni);
     m.part_cap = pc * B;
   }
-  for (int s = 16; s >= 4 && !m.num_slots; --s)
+  for (int s = 16; s >= 4 && !m.num_slots; s -= mk::kProducers)
     if (mk::smem_bytes_for(s, B, m.kmax, m.part_cap, cfg->hidden) <= cap) m.num_slots = s;
   if (!m.num_slots) return fail(MK_EINVAL, "activation rows (%d x %d) leave no room for the ring", B, m.kmax);
   m.smem = mk::smem_bytes_for(m.num_slots, B, m.kmax, m.part_cap, cfg->hidden);
+  if (int src = check_schedule_cached(cfg, B, sms, m.num_slots)) return src;
 
   // Scratch layout (as mk_init's), checked against the static array's size.
   const size_t H = cfg->hidden, I = cfg->intermediate, NQ = cfg->num_q_heads,
@@ -570,6 +656,17 @@ int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem
   if (grid) *grid = m->grid;
   if (ring_slots) *ring_slots = m->num_slots;
   if (smem_bytes) *smem_bytes = m->smem;
+  return MK_OK;
+}
+
+int mk_schedule_gap(const MkConfig* cfg, int32_t batch, int32_t grid, int32_t* gap) {
+  int rc = validate_config(cfg);
+  if (rc) return rc;
+  if (batch < 1 || batch > cfg->max_batch) return fail(MK_EINVAL, "batch %d outside [1, max_batch]", batch);
+  if (grid < 1) return fail(MK_EINVAL, "grid %d < 1", grid);
+  if (!gap) return fail(MK_EINVAL, "gap is NULL");
+  const int g = max_consumer_gap(cfg, batch, grid);
+  *gap = g == INT32_MAX ? -1 : g;
   return MK_OK;
 }
 

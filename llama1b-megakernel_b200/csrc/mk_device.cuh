@@ -23,6 +23,12 @@ constexpr int kAttnWarps = 8;              // warp states kept for the attention
 // .. + kProducers - 1), producer k taking the fills f with f % kProducers == k:
 // one lane issues at most ~50 GB/s of 16 KB bulk copies.
 constexpr int kProducers = 2;
+// Full barriers of the ring, used round-robin by the fills, so a barrier is
+// reused only every kFullBars fills; a producer issues fill f only once the
+// other has walked past fill f - kProducerSlack (see the Ring comment in
+// mk_kernel.cuh for why both bound a consumer warp's gap between waits).
+constexpr int kFullBars = 64;
+constexpr int kProducerSlack = 8;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + kProducers * 32;
 constexpr int kSegCols = 2048;             // max columns of one piece (a row segment)
@@ -31,7 +37,7 @@ constexpr int kSegCols = 2048;             // max columns of one piece (a row se
 constexpr int kAttnChunk = 4 * kConsumerWarps;
 static_assert(kAttnChunk * kHeadDim * 2 <= kSlotBytes / 2, "a chunk's K rows must fit half a slot");
 constexpr int kMaxSplit = 32;              // split-K pieces per (sequence, kv head)
-constexpr int kSplitMinPositions = 512;    // no split shorter than this (~9 chunks)
+constexpr int kSplitMinPositions = 128;    // no split shorter than this (~3 chunks)
 constexpr int kPartialStride = kHeadDim + 2;  // o[64], m, l per q head
 
 // Device error codes (error word [0]).
@@ -52,6 +58,16 @@ enum Counter : int {
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Shared-memory word handed between threads of the CTA with release/acquire order.
+__device__ __forceinline__ void st_release_shared(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_shared(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint64_t global_ns() {

@@ -134,7 +134,8 @@ struct SmemState {
   int pos[4];
   int n_split;
   int flag;
-  int pad[6];
+  uint32_t prod_pos[kProducers];  // fills each producer has walked past
+  int pad[4];
   float red[kConsumerWarps * 4];
   float am_val[kConsumerWarps * 4];
   int am_idx[kConsumerWarps * 4];
@@ -142,7 +143,7 @@ struct SmemState {
 
 // Shared-memory layout (dynamic): [ring S x 16 KB][x rows B x kmax bf16]
 // [partials part_cap fp32][raw residual B x H bf16][RoPE rows B x 128 bf16]
-// [attention scratch][mbarriers 2 x S][SmemState]
+// [attention scratch][mbarriers: kFullBars full, S empty][SmemState]
 constexpr int kAttnScratchBytes =
     kAttnWarps * kGroup * kPartialStride * 4 + kGroup * kHeadDim * 2 + 2 * kHeadDim * 4;
 
@@ -151,7 +152,7 @@ __host__ __device__ inline int align128(int x) { return (x + 127) & ~127; }
 __host__ __device__ inline int smem_bytes_for(int num_slots, int B, int kmax, int part_cap, int H) {
   return num_slots * kSlotBytes + align128(B * kmax * 2) + align128(part_cap * 4) +
          align128(B * H * 2) + align128(B * 2 * kHeadDim * 2) + kAttnScratchBytes +
-         2 * num_slots * 8 + (int)sizeof(SmemState) + 128;
+         (kFullBars + num_slots) * 8 + (int)sizeof(SmemState) + 128;
 }
 
 // Pieces per row of K columns: the fewest equal segments of at most
@@ -289,14 +290,16 @@ struct Split {
   int u0, u1;
 };
 
-__device__ __forceinline__ Split split_units(int U, int G, int c, int rot) {
+__host__ __device__ inline Split split_units(int U, int G, int c, int rot) {
   const int base = U / G, rem = U % G;
   const int end = rot + rem;
+  auto mn = [](int a, int b) { return a < b ? a : b; };
+  auto mx = [](int a, int b) { return a > b ? a : b; };
   int before;
   if (end <= G) {
-    before = min(max(c - rot, 0), rem);
+    before = mn(mx(c - rot, 0), rem);
   } else {
-    before = min(c, end - G) + min(max(c - rot, 0), G - rot);
+    before = mn(c, end - G) + mn(mx(c - rot, 0), G - rot);
   }
   const bool extra = ((c - rot + G) % G) < rem;
   const int u0 = c * base + before;
@@ -312,8 +315,8 @@ struct Sched {
   }
 };
 
-__device__ __forceinline__ int units_per_slot(int unit_bytes) {
-  return max(1, kSlotBytes / unit_bytes);
+__host__ __device__ inline int units_per_slot(int unit_bytes) {
+  return kSlotBytes / unit_bytes > 1 ? kSlotBytes / unit_bytes : 1;
 }
 
 // Item -> (seq, kv head, split) and its cached-position range [p0, p1).
@@ -374,11 +377,28 @@ __device__ void walk_schedule(const Params& p, const SmemState& st, Ops& ops) {
 
 // ---------------------------------------------------------------- ring
 
+// Fill f lands in slot f % S and completes full barrier f % kFullBars; its
+// readers release it on empty barrier f % S. An mbarrier wait names a phase
+// by parity only, so a consumer warp, which waits only for the fills it reads,
+// must never wait on a barrier whose previous phase is still open: it would
+// take the phase before that for its own and read a slot still being written.
+// Producer k issues fill f only once the other producer has walked past fill
+// f - kProducerSlack, so when any fill f' has landed, every fill up to
+// f' - kProducerSlack has been issued. A warp that waits for fill f after
+// waiting for fill f' with f - f' <= kFullBars - S - kProducerSlack therefore
+// knows fill f - kFullBars + S was issued, which its producer could only do
+// once the slot's earlier fill f - kFullBars had been read: that fill had
+// landed, and the barrier's previous phase is complete. (Fills below
+// kFullBars use fresh barriers.) The warp cannot be lapped either: it reads
+// fill f, so the slot is not refilled before it releases it. The host checks
+// the gap bound for every CTA's schedule before the first launch
+// (schedule_gap_ok in mk_api.cu); checking it here would cost the consumer
+// loop ~10% (measured).
 struct Ring {
   uint8_t* slots;    // generic address of slot 0
   uint32_t slots_s;  // shared-window address of slot 0
-  uint64_t* full;
-  uint64_t* empty;
+  uint64_t* full;    // [kFullBars]
+  uint64_t* empty;   // [S]
   int S;
   uint32_t n = 0;  // fills seen so far (the same count on every side)
   unsigned long long stall_ns = 0;  // time spent waiting (traced runs only)
@@ -421,8 +441,8 @@ __device__ __noinline__ bool ring_wait_slow(const Params& p, uint64_t* bar, uint
 
 // Consumer warp: wait until fill `f` has landed. false on abort/timeout.
 __device__ __forceinline__ bool ring_wait(const Params& p, Ring& r, uint32_t f, int where) {
-  uint64_t* bar = &r.full[f % r.S];
-  const uint32_t parity = (f / r.S) & 1;
+  uint64_t* bar = &r.full[f % kFullBars];
+  const uint32_t parity = (f / kFullBars) & 1;
   // try_wait may itself suspend the thread for a while, so a traced run
   // times the whole wait.
   const uint64_t ts = p.trace ? global_ns() : 0;
@@ -451,9 +471,34 @@ struct Producer {
 
   __device__ bool mine() const { return (int)(r.n % kProducers) == k; }
 
+  // Wait (bounded) until the other producer has walked past fill
+  // r.n - kProducerSlack (see the Ring comment). false on abort/timeout.
+  __device__ bool couple() {
+    const uint32_t* other = &st.prod_pos[k ^ 1];
+    if (ld_acquire_shared(other) + kProducerSlack > r.n) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0;; ++it) {
+      if (ld_acquire_shared(other) + kProducerSlack > r.n) {
+        if (p.trace) r.stall_ns += global_ns() - t0;
+        return true;
+      }
+      if ((it & 7) == 7) {
+        if (aborted(p)) return false;
+        if (global_ns() - t0 > p.timeout_ns) {
+          raise_error(p, kErrRingTimeout, 102);
+          return false;
+        }
+      }
+    }
+  }
+
   // Claim the next slot for `bytes` of transfers; nullptr when aborting.
   __device__ uint8_t* begin(uint32_t bytes) {
     if (!ok) return nullptr;
+    if (!couple()) {
+      ok = false;
+      return nullptr;
+    }
     const int slot = r.n % r.S;
     if (r.n >= (uint32_t)r.S) {
       const uint32_t parity = ((r.n / r.S) + 1) & 1;
@@ -464,11 +509,15 @@ struct Producer {
       }
       if (ts) r.stall_ns += global_ns() - ts;
     }
-    mbar_arrive_expect_tx(&r.full[slot], bytes);
+    mbar_arrive_expect_tx(bar(), bytes);
     return r.slots + (size_t)slot * kSlotBytes;
   }
-  __device__ uint64_t* bar() { return &r.full[r.n % r.S]; }
-  __device__ void end() { r.n++; }
+  __device__ uint64_t* bar() { return &r.full[r.n % kFullBars]; }
+  // Past fill r.n (issued, or the other producer's): publish the position.
+  __device__ void end() {
+    r.n++;
+    st_release_shared(&st.prod_pos[k], r.n);
+  }
 
   __device__ void mark(int ph, bool start) {
     if (!p.trace || k != 0) return;
@@ -486,7 +535,7 @@ struct Producer {
     const uint8_t* src = reinterpret_cast<const uint8_t*>(base);
     for (int u = sp.u0; u < sp.u1 && ok; u += ups) {
       if (!mine()) {
-        r.n++;
+        end();
         continue;
       }
       const int n = min(ups, sp.u1 - u);
@@ -502,7 +551,7 @@ struct Producer {
   // K into the slot's first 8 KB and V into its second.
   __device__ void kv_chunk(int layer, int b, int g, int c0, int n) {
     if (!mine()) {
-      r.n++;
+      end();
       return;
     }
     uint8_t* dst = begin((uint32_t)n * 2 * kHeadDim * 2);
@@ -537,7 +586,8 @@ struct Producer {
   __device__ void drain() {
     const uint32_t first = r.n > (uint32_t)r.S ? r.n - r.S : 0;
     for (uint32_t f = first; f < r.n; ++f) {
-      if ((int)(f % kProducers) == k) mbar_wait(p, &r.full[f % r.S], (f / r.S) & 1, -1, 2 * p.timeout_ns);
+      if ((int)(f % kProducers) == k)
+        mbar_wait(p, &r.full[f % kFullBars], (f / kFullBars) & 1, -1, 2 * p.timeout_ns);
     }
   }
 };
@@ -1402,15 +1452,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   float* kvn = reinterpret_cast<float*>(qs + kGroup * kHeadDim);
   cur += kAttnScratchBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(cur);
-  SmemState* st = reinterpret_cast<SmemState*>(bars + 2 * S);
+  SmemState* st = reinterpret_cast<SmemState*>(bars + kFullBars + S);
 
-  Ring ring{ring_mem, smem_addr(ring_mem), bars, bars + S, S};
+  Ring ring{ring_mem, smem_addr(ring_mem), bars, bars + kFullBars, S};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&ring.full[s], 1);
-      mbar_init(&ring.empty[s], kConsumerWarps);
-    }
+    for (int s = 0; s < kFullBars; ++s) mbar_init(&ring.full[s], 1);
+    for (int s = 0; s < S; ++s) mbar_init(&ring.empty[s], kConsumerWarps);
     fence_mbar_init();
     int pmax = 0;
     bool bad = false;
@@ -1435,6 +1483,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     ns = max(1, min(ns, (pmax + kSplitMinPositions - 1) / kSplitMinPositions));
     st->n_split = ns;
     st->flag = bad ? 1 : 0;
+    for (int k = 0; k < kProducers; ++k) st->prod_pos[k] = 0;
   }
   __syncthreads();
   if (st->flag) return;

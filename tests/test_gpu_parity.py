@@ -23,7 +23,7 @@ import pytest
 import torch
 
 from llama1b_megakernel_b200 import synthetic as syn
-from llama1b_megakernel_b200.config import LLAMA_3_2_1B, SMALL, TINY
+from llama1b_megakernel_b200.config import LLAMA_3_2_1B, MID, SMALL, TINY
 from oracle import llama_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -205,6 +205,37 @@ def test_small_generate_feedback_matches_forward(small_w):
         out = m.forward(torch.tensor([[toks[-1]]]), past_key_values=kv)
         toks.append(int(out.next_ids[0]))
     assert gen[0].tolist() == toks
+
+
+# ----------------------------------------------------------------------------
+# MID: two Llama-3.2-1B-shaped layers with a small vocabulary
+# ----------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def mid_w():
+    return syn.make_weights(MID, seed=23)
+
+
+@pytest.fixture(scope="module")
+def mid_w32(mid_w):
+    return _fp32_copy(mid_w)
+
+
+@pytest.mark.parametrize("pos", [0, 1, 47, 48, 130, 600])
+def test_mid_single_step_positions(mid_w, mid_w32, pos):
+    _run_step_case(MID, mid_w, 1, [pos], page_size=64, seed=pos + 3, w32=mid_w32)
+
+
+def test_mid_batched_ragged(mid_w, mid_w32):
+    _run_step_case(MID, mid_w, 2, [300, 17], page_size=32, seed=4, w32=mid_w32)
+
+
+def test_mid_multistep_deterministic(mid_w):
+    m = _model(MID, mid_w, 1, max_seq_len=128, page_size=64)
+    toks = syn.random_tokens(6, MID.vocab, seed=13)
+    a = m.forward(toks.reshape(1, 6), past_key_values=m.new_cache())
+    b = m.forward(toks.reshape(1, 6), past_key_values=m.new_cache())
+    assert torch.equal(a.logits, b.logits) and torch.equal(a.next_ids, b.next_ids)
 
 
 # ----------------------------------------------------------------------------
