@@ -20,8 +20,12 @@ against the measured HBM copy bandwidth in MEASURED_PEAKS.json.
 ``LlamaForCausalLM``, via oracle/) timed on the host CPU cores on a bounded
 sample of the same workload; rank 0 only.
 
-Multi-GPU (torchrun, N > 1): N independent replicas, one per GPU (weak
-scaling); ``value`` = total tokens/s of all ranks.
+Multi-GPU (torchrun, N > 1): tensor-parallel decode
+of the one sequence over the N GPUs (``TensorParallelLlamaForCausalLM``: q/kv
+heads, MLP rows and lm_head rows sharded, partial sums exchanged inside the
+kernel over NVLink); ``value`` = tokens/s of that sequence (strong scaling),
+the step time being the max over ranks. ``--replicas`` runs N independent
+single-GPU replicas instead (weak scaling, total tokens/s).
 """
 from __future__ import annotations
 
@@ -52,6 +56,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=640)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent replicas instead of tensor parallelism")
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--no-sweep", action="store_true", help="skip the ctx sweep extra")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -253,11 +259,18 @@ def run_ours(args, ws, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     hbm_peak, peak_kind = peaks()
-    sweep = not (args.no_sweep or args.small)
+    tp_world = ws if (ws > 1 and not args.replicas) else 1
+    sweep = not (args.no_sweep or args.small) and tp_world == 1
     max_seq = 8192 + 64 if sweep else MAX_CTX
     w = syn.make_weights(cfg, seed=0, device=dev)
-    model = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=max_seq, page_size=64,
-                                       device=dev)
+    if tp_world > 1:
+        from llama1b_megakernel_b200.tp import TensorParallelLlamaForCausalLM
+
+        model = TensorParallelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=max_seq,
+                                               page_size=64, device=dev)
+    else:
+        model = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=max_seq,
+                                           page_size=64, device=dev)
     w_cpu = None
     if rank == 0 and ws == 1 and not (args.no_cpu_baseline or args.small):
         w_cpu = {k: t.cpu() for k, t in w.items()}
@@ -304,15 +317,16 @@ def run_ours(args, ws, rank, local):
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = starts[0].elapsed_time(ends[-1])
     total_ms = max_over_ranks(total_ms, ws)
-    tokens_all = K * ws
-    value = tokens_all / (total_ms / 1e3)
+    seqs = ws // tp_world  # sequences decoded by the whole job
+    value = K * seqs / (total_ms / 1e3)
     p50 = statistics.median(step_ms)
     p90 = sorted(step_ms)[int(0.9 * (K - 1))]
     p99 = sorted(step_ms)[int(0.99 * (K - 1))]
     kernel_ms = statistics.mean(step_ms)
     ctx_mean = PROMPT_LEN + (K - 1) / 2.0
-    bytes_step = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_position() * ctx_mean + \
-        cfg.kv_bytes_per_position()
+    # per GPU: a tensor-parallel rank streams 1/tp_world of the weights and KV
+    bytes_step = (cfg.weight_bytes_per_token() + cfg.kv_bytes_per_position() * ctx_mean +
+                  cfg.kv_bytes_per_position()) / tp_world
     achieved = bytes_step / (kernel_ms / 1e3) / 1e9
 
     # ------------------------------------------------------------ e2e (public API)
@@ -339,7 +353,7 @@ def run_ours(args, ws, rank, local):
             ids[0, 0] = int(o.next_ids[0])  # D2H of the result, host feeds it back
         t1 = time.perf_counter()
         e2e_s = max_over_ranks(t1 - t0, ws)
-        e2e_val = n * ws / e2e_s
+        e2e_val = n * seqs / e2e_s
         h2d = 2 * 4   # token id + position (int32) per step
         d2h = 4       # next id (int32) per step
 
@@ -389,16 +403,18 @@ def run_ours(args, ws, rank, local):
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K,
             "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if tp_world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, seeded random prompt)",
             "config": {"workload": "Llama-3.2-1B bs=1 greedy decode: 128-token prompt, then "
                                    f"{K} steps from position 128 (max ctx 1024)",
-                       "global_batch": ws, "seq_len": MAX_CTX, "parallelism": f"replicas x{ws}",
+                       "global_batch": seqs, "seq_len": MAX_CTX,
+                       "parallelism": f"tp{tp_world}" if tp_world > 1 else f"replicas x{ws}",
                        "l2": "inputs larger than L2 (2.47 GB of weights streamed per step)"},
             "p50_ms": p50, "p90_ms": p90, "p99_ms": p99,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
                          "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "traffic": traffic_summary(),
+                         "peak_kind": peak_kind,
+                         "traffic": traffic_summary() if tp_world == 1 else None,
                          "bytes_per_step": bytes_step},
             "frac_of_8tbs": achieved / 8000.0,
             "clocks": clk,

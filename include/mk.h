@@ -202,6 +202,38 @@ int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed
 /* Launch geometry chosen by mk_init: CTAs (one per SM) and ring slots per CTA. */
 int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem_bytes);
 
+/* ---- Tensor parallelism (one decode step over `world` GPUs) --------------
+ *
+ * Each rank's handle is made with mk_init from the rank's LOCAL geometry:
+ * num_q_heads / world q heads, num_kv_heads / world kv heads and
+ * intermediate / world MLP rows (vocab stays the whole vocabulary), and its
+ * weights are that rank's shard: the q/k/v rows of its heads, the o_proj
+ * columns of its q heads, the gate/up rows and down columns of its MLP rows,
+ * the whole embedding table (token lookup) of which it scores lm_head rows
+ * [lm_row0, lm_row0 + lm_rows). Its KV cache holds only its kv heads. After
+ * o_proj and down every rank sends its fp32 partial sums to every other
+ * rank's exchange buffer over NVLink inside the kernel and all ranks add them
+ * in rank order, so they carry identical residuals; the greedy argmax is
+ * exchanged the same way. Logits written by mk_decode are the rank's slice,
+ * [batch][lm_rows]. All ranks must make the same sequence of launches.
+ * Replaces the all-reduces a tensor-parallel NxDI decoder would issue (the
+ * reference's megakernel itself asserts TP = 1, llama_with_megakernel.py:145-149). */
+typedef struct MkIpcHandle {
+  unsigned char bytes[64]; /* a cudaIpcMemHandle_t */
+} MkIpcHandle;
+
+/* Make `m` rank `rank` of `world` scoring lm_head rows [lm_row0, lm_row0 +
+ * lm_rows); allocates its exchange buffer (world > 1) and returns its IPC
+ * handle and device address (either may be NULL). world == 1 only restricts
+ * the lm_head rows. */
+int mk_tp_setup(MkModel* m, int32_t rank, int32_t world, int32_t lm_row0, int32_t lm_rows,
+                MkIpcHandle* handle, void** buffer);
+
+/* Map the other ranks' exchange buffers: `handles[world]` from their
+ * mk_tp_setup when each rank is its own process, or `buffers[world]` when one
+ * process drives all GPUs (peer access is enabled); exactly one non-NULL. */
+int mk_tp_connect(MkModel* m, const MkIpcHandle* handles, void* const* buffers);
+
 /* The largest number of ring fills a consumer warp goes between two waits in
  * the kernel's schedule for this geometry, batch and grid (-1 if a warp's
  * first wait comes at fill 64 or later). mk_init refuses a geometry whose gap

@@ -24,7 +24,7 @@ STATUS_NAMES = {
 EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
-    "mk_query", "mk_schedule_gap", "mk_last_error", "mk_destroy",
+    "mk_query", "mk_schedule_gap", "mk_tp_setup", "mk_tp_connect", "mk_last_error", "mk_destroy",
 )
 
 
@@ -52,6 +52,10 @@ class MkWeights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "embed", "w_qkv", "w_o", "w_gate_up", "w_down", "norm_attn", "norm_mlp",
         "norm_final", "rope_cos", "rope_sin")]
+
+
+class MkIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 class MkKVCache(ctypes.Structure):
@@ -85,6 +89,8 @@ def load() -> ctypes.CDLL:
     lib.mk_set_trace.argtypes = [VP, VP, ctypes.c_int64, P(ctypes.c_int64)]
     lib.mk_query.argtypes = [VP, P(I32), P(I32), P(I32)]
     lib.mk_schedule_gap.argtypes = [P(MkConfig), I32, I32, P(I32)]
+    lib.mk_tp_setup.argtypes = [VP, I32, I32, I32, I32, P(MkIpcHandle), P(VP)]
+    lib.mk_tp_connect.argtypes = [VP, P(MkIpcHandle), P(VP)]
     lib.mk_last_error.argtypes = []
     lib.mk_last_error.restype = ctypes.c_char_p
     lib.mk_destroy.argtypes = [VP]

@@ -72,6 +72,13 @@ struct MkModel {
   int* host_error_dev = nullptr;  // its device address
   size_t counters_bytes = 0;
   unsigned long long* trace = nullptr;  // borrowed, see mk_set_trace
+  // tensor parallelism (mk_tp_setup / mk_tp_connect)
+  int tp_rank = 0, tp_world = 1;
+  int lm_row0 = 0, lm_rows = -1;  // -1: the whole vocabulary
+  unsigned long long* xbuf = nullptr;  // this rank's exchange buffer
+  unsigned long long* xpeer[mk::kMaxTp] = {};
+  bool xpeer_ipc[mk::kMaxTp] = {};  // opened with cudaIpcOpenMemHandle (closed on destroy)
+  bool tp_connected = false;
 };
 
 namespace {
@@ -90,7 +97,7 @@ namespace {
 // chunks are read by every warp except the last, partial chunk of an item, so
 // each attention item of the CTA counts as one fill no warp reads; the item
 // count is its maximum over positions.
-int max_consumer_gap(const MkConfig* c, int B, int G) {
+int max_consumer_gap(const MkConfig* c, int B, int G, int lm_rows) {
   constexpr int NC = mk::kConsumerWarps;
   const int H = c->hidden, I = c->intermediate, QD = c->num_q_heads * 64;
   const int NQKV = c->num_q_heads + 2 * c->num_kv_heads;
@@ -125,16 +132,16 @@ int max_consumer_gap(const MkConfig* c, int B, int G) {
       gemv(I, 4 * H, 2 * nh);
       gemv(H, 2 * I, ni);
     }
-    gemv(c->vocab, 2 * H, 1);
+    gemv(lm_rows, 2 * H, 1);
   }
   return worst;
 }
 
 // Every batch a launch may use (1 .. max_batch) has its own schedule.
-int check_schedule(const MkConfig* c, int max_batch, int G, int S) {
+int check_schedule(const MkConfig* c, int max_batch, int G, int S, int lm_rows = -1) {
   const int bound = mk::kFullBars - S - mk::kProducerSlack;
   for (int B = 1; B <= max_batch; ++B) {
-    const int gap = max_consumer_gap(c, B, G);
+    const int gap = max_consumer_gap(c, B, G, lm_rows < 0 ? c->vocab : lm_rows);
     if (gap > bound)
       return fail(MK_EINVAL, "fill schedule at batch %d: a consumer warp would go %d fills between "
                   "ring waits (at most %d are safe with %d slots)", B,
@@ -226,6 +233,8 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
             int32_t* next_ids, int32_t flags, void* stream) {
   if (!m) return fail(MK_EINVAL, "model is NULL");
   if (!m->has_weights) return fail(MK_ESTATE, "mk_load_weights has not been called");
+  if (m->tp_world > 1 && !m->tp_connected)
+    return fail(MK_ESTATE, "tensor-parallel rank: mk_tp_connect has not been called");
   if (batch < 1 || batch > m->cfg.max_batch)
     return fail(MK_EINVAL, "batch %d outside [1, max_batch=%d]", batch, m->cfg.max_batch);
   if (!positions) return fail(MK_EINVAL, "positions is NULL");
@@ -297,6 +306,11 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   p.tag_base = (uint32_t)(((uint64_t)m->launch_seq++ * (uint64_t)(5 * c.num_layers + 1)) % 65535u);
   p.trace = m->trace;
   p.trace_per_cta = (c.num_layers * 5 + 1) * mk::kTraceKinds;
+  p.tp_rank = m->tp_rank;
+  p.tp_world = m->tp_world;
+  p.lm_row0 = m->lm_row0;
+  p.lm_rows = m->lm_rows < 0 ? c.vocab : m->lm_rows;
+  for (int r = 0; r < mk::kMaxTp; ++r) p.xpeer[r] = m->xpeer[r];
   MK_CUDA(dispatch_launch(batch, p, m->grid, m->smem, static_cast<cudaStream_t>(stream)));
   return MK_OK;
 }
@@ -665,16 +679,96 @@ int mk_schedule_gap(const MkConfig* cfg, int32_t batch, int32_t grid, int32_t* g
   if (batch < 1 || batch > cfg->max_batch) return fail(MK_EINVAL, "batch %d outside [1, max_batch]", batch);
   if (grid < 1) return fail(MK_EINVAL, "grid %d < 1", grid);
   if (!gap) return fail(MK_EINVAL, "gap is NULL");
-  const int g = max_consumer_gap(cfg, batch, grid);
+  const int g = max_consumer_gap(cfg, batch, grid, cfg->vocab);
   *gap = g == INT32_MAX ? -1 : g;
   return MK_OK;
 }
 
 const char* mk_last_error(void) { return g_last_error.c_str(); }
 
+int mk_tp_setup(MkModel* m, int32_t rank, int32_t world, int32_t lm_row0, int32_t lm_rows,
+                MkIpcHandle* handle, void** buffer) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (world < 1 || world > mk::kMaxTp) return fail(MK_EINVAL, "world %d outside [1, %d]", world, mk::kMaxTp);
+  if (rank < 0 || rank >= world) return fail(MK_EINVAL, "rank %d outside [0, %d)", rank, world);
+  if (lm_row0 < 0 || lm_rows < 1 || (long long)lm_row0 + lm_rows > m->cfg.vocab)
+    return fail(MK_EINVAL, "lm_head rows [%d, %d + %d) outside the vocabulary (%d)", lm_row0, lm_row0,
+                lm_rows, m->cfg.vocab);
+  if (m->xbuf || m->tp_connected) return fail(MK_ESTATE, "mk_tp_setup was already called");
+  if (int rc = check_schedule(&m->cfg, m->cfg.max_batch, m->num_sms, m->num_slots, lm_rows)) return rc;
+  MK_CUDA(cudaSetDevice(m->device));
+  m->tp_rank = rank;
+  m->tp_world = world;
+  m->lm_row0 = lm_row0;
+  m->lm_rows = lm_rows;
+  if (world == 1) {
+    m->xpeer[0] = nullptr;
+    m->tp_connected = true;
+    if (buffer) *buffer = nullptr;
+    if (handle) memset(handle, 0, sizeof(*handle));
+    return MK_OK;
+  }
+  const size_t bytes = mk::xbuf_words(world, m->cfg.max_batch, m->cfg.hidden) * 8;
+  void* buf = nullptr;
+  MK_CUDA(cudaMalloc(&buf, bytes));
+  m->xbuf = static_cast<unsigned long long*>(buf);
+  MK_CUDA(cudaMemset(buf, 0, bytes));  // tag 0 is never a phase tag
+  MK_CUDA(cudaDeviceSynchronize());
+  if (handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(MkIpcHandle), "IPC handle size");
+    cudaIpcMemHandle_t h;
+    MK_CUDA(cudaIpcGetMemHandle(&h, buf));
+    memcpy(handle, &h, sizeof(h));
+  }
+  if (buffer) *buffer = buf;
+  return MK_OK;
+}
+
+int mk_tp_connect(MkModel* m, const MkIpcHandle* handles, void* const* buffers) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (m->tp_world == 1) return m->tp_connected ? MK_OK : fail(MK_ESTATE, "mk_tp_setup has not been called");
+  if (!m->xbuf) return fail(MK_ESTATE, "mk_tp_setup has not been called");
+  if (m->tp_connected) return fail(MK_ESTATE, "mk_tp_connect was already called");
+  if ((handles == nullptr) == (buffers == nullptr))
+    return fail(MK_EINVAL, "pass exactly one of handles (one process per GPU) and buffers (one process)");
+  MK_CUDA(cudaSetDevice(m->device));
+  for (int r = 0; r < m->tp_world; ++r) {
+    if (r == m->tp_rank) {
+      m->xpeer[r] = m->xbuf;
+      continue;
+    }
+    void* ptr = nullptr;
+    if (handles) {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, &handles[r], sizeof(h));
+      MK_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+      m->xpeer_ipc[r] = true;
+    } else {
+      ptr = buffers[r];
+      if (!ptr) return fail(MK_EINVAL, "buffers[%d] is NULL", r);
+      cudaPointerAttributes a;
+      MK_CUDA(cudaPointerGetAttributes(&a, ptr));
+      if (a.device != m->device) {
+        const cudaError_t e = cudaDeviceEnablePeerAccess(a.device, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) {
+          cudaGetLastError();
+        } else if (e != cudaSuccess) {
+          return fail(MK_ECUDA, "peer access to device %d: %s", a.device, cudaGetErrorString(e));
+        }
+      }
+    }
+    m->xpeer[r] = static_cast<unsigned long long*>(ptr);
+  }
+  m->tp_connected = true;
+  return MK_OK;
+}
+
 int mk_destroy(MkModel* m) {
   if (!m) return MK_OK;
   cudaSetDevice(m->device);
+  for (int r = 0; r < mk::kMaxTp; ++r)
+    if (m->xpeer_ipc[r] && m->xpeer[r]) cudaIpcCloseMemHandle(m->xpeer[r]);
+  if (m->xbuf) cudaFree(m->xbuf);
   if (m->scratch) cudaFree(m->scratch);
   if (m->host_error) cudaFreeHost(m->host_error);
   delete m;

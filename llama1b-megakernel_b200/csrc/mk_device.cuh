@@ -29,6 +29,8 @@ constexpr int kProducers = 2;
 // mk_kernel.cuh for why both bound a consumer warp's gap between waits).
 constexpr int kFullBars = 64;
 constexpr int kProducerSlack = 8;
+// Tensor parallelism: at most this many GPUs share one decode step.
+constexpr int kMaxTp = 8;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + kProducers * 32;
 constexpr int kSegCols = 2048;             // max columns of one piece (a row segment)
@@ -58,6 +60,25 @@ enum Counter : int {
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 64-bit words exchanged with the other GPUs of a tensor-parallel group
+// (peer memory mapped through CUDA IPC, carried by NVLink): system scope.
+__device__ __forceinline__ void st_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Shared-memory word handed between threads of the CTA with release/acquire order.

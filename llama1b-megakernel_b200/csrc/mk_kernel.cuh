@@ -104,7 +104,30 @@ struct Params {
   // optional phase trace ([grid][trace_per_cta] u64, see kTrace*); nullptr = off
   unsigned long long* trace;
   int trace_per_cta;
+  // Tensor parallelism over tp_world GPUs (1: none). This rank holds NQ q
+  // heads, NKV kv heads and I MLP rows of the model (the counts above are the
+  // local ones) and scores lm_head rows [lm_row0, lm_row0 + lm_rows); V is
+  // the whole vocabulary. xpeer[r] is rank r's exchange buffer as mapped on
+  // this GPU (xpeer[tp_rank] is this rank's own; see xbuf_* for its layout).
+  int tp_rank, tp_world;
+  int lm_row0, lm_rows;
+  unsigned long long* xpeer[kMaxTp];
 };
+
+// Exchange buffer of a tensor-parallel rank, 64-bit words written by every
+// rank of the group: o_proj and down partial sums, [2][tp_world][B][H] words
+// (tag << 32 | fp32 bits), then the lm_head argmax keys [tp_world][B], then
+// one "keys published" flag word per rank (the tag).
+__host__ __device__ inline size_t xbuf_partial(int slot, int src, int b, int u, int W, int B, int H) {
+  return (((size_t)slot * W + src) * B + b) * H + u;
+}
+__host__ __device__ inline size_t xbuf_keys(int src, int b, int W, int B, int H) {
+  return (size_t)2 * W * B * H + (size_t)src * B + b;
+}
+__host__ __device__ inline size_t xbuf_flag(int src, int W, int B, int H) {
+  return (size_t)2 * W * B * H + (size_t)W * B + src;
+}
+__host__ __device__ inline size_t xbuf_words(int W, int B, int H) { return xbuf_flag(W, W, B, H); }
 
 // Phase trace. Phase index: layer * 5 + {0 QKV, 1 ATTN, 2 O, 3 GU, 4 DOWN},
 // num_layers * 5 = LM head. Per (CTA, phase) kTraceKinds u64 entries:
@@ -245,6 +268,85 @@ __device__ __forceinline__ uint2 untag4(const uint4& u) {
   return make_uint2((u.x >> 16) | (u.y & 0xFFFF0000u), (u.z >> 16) | (u.w & 0xFFFF0000u));
 }
 
+// ---------------------------------------------------------------- tensor parallelism
+//
+// The o_proj and down projections are split over the group by their input
+// columns (each rank holds its q heads' o_proj columns and its MLP rows'
+// down columns), so every rank has a partial sum of every output row. The
+// CTA that owns row u on each rank publishes its fp32 partial, tagged with
+// the phase, to every rank's exchange buffer (peer stores over NVLink), then
+// reads the tp_world partials of u from its own buffer and adds them in rank
+// order, so every rank computes the same residual bit for bit and publishes
+// it locally as a tagged activation, as a single GPU does.
+
+__device__ __forceinline__ void tp_publish(const Params& p, int slot, int b, int u, float mine,
+                                           uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(mine);
+  for (int r = 0; r < p.tp_world; ++r)
+    st_sys_u64(p.xpeer[r] + xbuf_partial(slot, p.tp_rank, b, u, p.tp_world, p.B, p.H), w);
+}
+
+struct Summed {
+  float v;
+  int ok;
+};
+
+// Sum over ranks of row u's partials (time-bounded wait for each).
+__device__ __noinline__ Summed tp_sum(const Params& p, int slot, int b, int u, uint32_t tag,
+                                      int where) {
+  const unsigned long long* own = p.xpeer[p.tp_rank];
+  float acc = 0.f;
+  uint64_t t0 = 0;
+  for (int r = 0; r < p.tp_world; ++r) {
+    const unsigned long long* w = own + xbuf_partial(slot, r, b, u, p.tp_world, p.B, p.H);
+    unsigned long long v = ld_sys_u64(w);
+    for (uint32_t it = 1; (uint32_t)(v >> 32) != tag; ++it) {
+      if (!t0) t0 = global_ns();
+      __nanosleep(64);
+      v = ld_sys_u64(w);
+      if ((it & 15) == 0) {
+        if (aborted(p)) return {0.f, 0};
+        if (global_ns() - t0 > p.timeout_ns) {
+          raise_error(p, kErrBarrierTimeout, where);
+          return {0.f, 0};
+        }
+      }
+    }
+    acc += __uint_as_float((uint32_t)v);
+  }
+  return {acc, 1};
+}
+
+// The group's argmax: publish this rank's packed keys (B of them) and a flag
+// to every rank, wait (bounded) for every rank's flag, and fold the keys into
+// `key` (max: highest logit, lowest index). false on abort or timeout.
+__device__ __noinline__ bool tp_argmax(const Params& p, unsigned long long* key, uint32_t tag) {
+  const int W = p.tp_world, B = p.B, H = p.H;
+  for (int r = 0; r < W; ++r)
+    for (int b = 0; b < B; ++b) st_sys_u64(p.xpeer[r] + xbuf_keys(p.tp_rank, b, W, B, H), key[b]);
+  __threadfence_system();
+  for (int r = 0; r < W; ++r) st_release_sys_u64(p.xpeer[r] + xbuf_flag(p.tp_rank, W, B, H), tag);
+  const unsigned long long* own = p.xpeer[p.tp_rank];
+  const uint64_t t0 = global_ns();
+  for (int r = 0; r < W; ++r) {
+    for (uint32_t it = 1; ld_acquire_sys_u64(own + xbuf_flag(r, W, B, H)) != tag; ++it) {
+      __nanosleep(64);
+      if ((it & 15) == 0) {
+        if (aborted(p)) return false;
+        if (global_ns() - t0 > p.timeout_ns) {
+          raise_error(p, kErrBarrierTimeout, 12000 + r);
+          return false;
+        }
+      }
+    }
+    for (int b = 0; b < B; ++b) {
+      const unsigned long long k = ld_sys_u64(own + xbuf_keys(r, b, W, B, H));
+      if (k > key[b]) key[b] = k;
+    }
+  }
+  return true;
+}
+
 // Spin until *c >= target (wrap-safe). false on timeout or abort.
 __device__ __noinline__ bool counter_wait(const Params& p, const uint32_t* c, uint32_t target,
                                           int where) {
@@ -370,7 +472,7 @@ __device__ void walk_schedule(const Params& p, const SmemState& st, Ops& ops) {
   }
   if (p.mode == 0 && ops.ok) {
     ops.mark(p.L * 5, true);
-    ops.units(p.embed, 2 * H, sch.next(p.V));
+    ops.units(p.embed + (size_t)p.lm_row0 * H, 2 * H, sch.next(p.lm_rows));
     ops.mark(p.L * 5, false);
   }
 }
@@ -1155,19 +1257,19 @@ struct ToPart {
 // argmax (lowest index on ties), kept by lane 0.
 template <int B>
 struct LmOut {
-  float* logits;
-  int V, u0;
+  float* logits;  // [B][rows]: this rank's lm_head rows
+  int rows, u0, row0;  // row u of the slice is vocabulary id row0 + u
   float best_v[B];
   int best_i[B];
   __device__ void operator()(int t, const float (&v)[B], int lane) {
     if (lane != 0) return;
-    const int u = u0 + t;
+    const int u = u0 + t, id = row0 + u;
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      if (logits) logits[(size_t)b * V + u] = v[b];
-      if (v[b] > best_v[b] || (v[b] == best_v[b] && u < best_i[b])) {
+      if (logits) logits[(size_t)b * rows + u] = v[b];
+      if (v[b] > best_v[b] || (v[b] == best_v[b] && id < best_i[b])) {
         best_v[b] = v[b];
-        best_i[b] = u;
+        best_i[b] = id;
       }
     }
   }
@@ -1292,11 +1394,25 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       ok = gemv_phase<B>(p, ring, xs_s, QD, p.nseg_qd, 1, 1, so, 5000 + l, to_part);
       if (consumer_any(!ok)) return;
       const int nu = so.u1 - so.u0, ns = p.nseg_qd;
-      for (int i = tid; i < nu * B; i += kConsumerThreads) {
-        const int ul = i / B, b = i % B, u = so.u0 + ul;
-        // residual: the layer input, kept raw by the QKV phase's row load
-        const float r = bf2f(raw[b * H + u]);
-        p.h[(size_t)b * H + u] = tagged(r + rbf(row_sum(ul * ns, ns, b)), phase_tag(p, l * 5 + 2));
+      const uint32_t tag = phase_tag(p, l * 5 + 2);
+      if (p.tp_world > 1) {
+        for (int i = tid; i < nu * B; i += kConsumerThreads)
+          tp_publish(p, 0, i % B, so.u0 + i / B, row_sum((i / B) * ns, ns, i % B), tag);
+        int good = 1;
+        for (int i = tid; i < nu * B && good; i += kConsumerThreads) {
+          const int b = i % B, u = so.u0 + i / B;
+          const Summed o = tp_sum(p, 0, b, u, tag, 4500 + l);
+          good = o.ok;
+          p.h[(size_t)b * H + u] = tagged(bf2f(raw[b * H + u]) + rbf(o.v), tag);
+        }
+        if (consumer_any(!good)) return;
+      } else {
+        for (int i = tid; i < nu * B; i += kConsumerThreads) {
+          const int ul = i / B, b = i % B, u = so.u0 + ul;
+          // residual: the layer input, kept raw by the QKV phase's row load
+          const float r = bf2f(raw[b * H + u]);
+          p.h[(size_t)b * H + u] = tagged(r + rbf(row_sum(ul * ns, ns, b)), tag);
+        }
       }
     }
     mark_done(l * 5 + 2);
@@ -1346,13 +1462,29 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       ok = gemv_phase<B>(p, ring, xs_s, I, p.nseg_i, 1, 1, sd, 9000 + l, to_part);
       if (consumer_any(!ok)) return;
       const int nu = sd.u1 - sd.u0, ns = p.nseg_i;
-      for (int i = tid; i < nu * B; i += kConsumerThreads) {
-        const int ul = i / B, b = i % B, u = sd.u0 + ul;
-        // residual: h after o_proj, kept raw by the GU phase's row load
-        const float r = bf2f(raw[b * H + u]);
-        const float y = r + rbf(row_sum(ul * ns, ns, b));
-        p.h[(size_t)b * H + u] = tagged(y, phase_tag(p, l * 5 + 4));
-        if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = f2bf(y);
+      const uint32_t tag = phase_tag(p, l * 5 + 4);
+      if (p.tp_world > 1) {
+        for (int i = tid; i < nu * B; i += kConsumerThreads)
+          tp_publish(p, 1, i % B, sd.u0 + i / B, row_sum((i / B) * ns, ns, i % B), tag);
+        int good = 1;
+        for (int i = tid; i < nu * B && good; i += kConsumerThreads) {
+          const int b = i % B, u = sd.u0 + i / B;
+          const Summed d = tp_sum(p, 1, b, u, tag, 8500 + l);
+          good = d.ok;
+          const float y = bf2f(raw[b * H + u]) + rbf(d.v);
+          p.h[(size_t)b * H + u] = tagged(y, tag);
+          if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = f2bf(y);
+        }
+        if (consumer_any(!good)) return;
+      } else {
+        for (int i = tid; i < nu * B; i += kConsumerThreads) {
+          const int ul = i / B, b = i % B, u = sd.u0 + ul;
+          // residual: h after o_proj, kept raw by the GU phase's row load
+          const float r = bf2f(raw[b * H + u]);
+          const float y = r + rbf(row_sum(ul * ns, ns, b));
+          p.h[(size_t)b * H + u] = tagged(y, tag);
+          if (last_layer && p.mode == 1) p.hidden_out[(size_t)b * H + u] = f2bf(y);
+        }
       }
     }
     mark_done(l * 5 + 4);
@@ -1371,8 +1503,8 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
         return;
     }
     mark(p.L * 5, kTrRowsLoaded);
-    const Split sl = sch.next(p.V);
-    LmOut<B> lm{p.logits, p.V, sl.u0};
+    const Split sl = sch.next(p.lm_rows);
+    LmOut<B> lm{p.logits, p.lm_rows, sl.u0, p.lm_row0};
 #pragma unroll
     for (int b = 0; b < B; ++b) {
       lm.best_v[b] = -INFINITY;
@@ -1416,13 +1548,16 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
     const uint32_t t = atom_add_acq_rel_u32(p.counters + kCntDone, 1u);
     if (t == gridDim.x - 1) {
       if (p.mode == 0) {
-        for (int b = 0; b < B; ++b) {
-          const unsigned long long key = atomicExch(p.keys + b, 0ull);
-          const int id = (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
-          p.next_ids[b] = id;
-          if (p.flags & 1) {
-            p.tokens[b] = id;
-            p.positions[b] = st.pos[b] + 1;
+        unsigned long long key[B];
+        for (int b = 0; b < B; ++b) key[b] = atomicExch(p.keys + b, 0ull);
+        if (p.tp_world == 1 || tp_argmax(p, key, phase_tag(p, p.L * 5))) {
+          for (int b = 0; b < B; ++b) {
+            const int id = (int)(0xFFFFFFFFu - (uint32_t)(key[b] & 0xFFFFFFFFull));
+            p.next_ids[b] = id;
+            if (p.flags & 1) {
+              p.tokens[b] = id;
+              p.positions[b] = st.pos[b] + 1;
+            }
           }
         }
       }

@@ -35,7 +35,7 @@ class DecodeOutput:
 class MegakernelLlamaForCausalLM(torch.nn.Module):
     def __init__(self, cfg: LlamaDecodeConfig, state_dict: dict, max_batch: int = 1,
                  max_seq_len: int = 2048, page_size: int = 64, device="cuda",
-                 rope_len: int | None = None):
+                 rope_len: int | None = None, lm_rows: int | None = None):
         super().__init__()
         if not torch.cuda.is_available():
             raise RuntimeError("MegakernelLlamaForCausalLM needs a CUDA device (sm_100a)")
@@ -55,7 +55,10 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
             self._tokens = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
             self._positions = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
             self._next = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
-            self._logits = torch.empty(max_batch, cfg.vocab, dtype=torch.float32, device=self.device)
+            # lm_head rows this model scores (a tensor-parallel rank scores a slice)
+            self.lm_rows = lm_rows or cfg.vocab
+            self._logits = torch.empty(max_batch, self.lm_rows, dtype=torch.float32,
+                                       device=self.device)
         self._handle = ctypes.c_void_p()
         c = _lib.MkConfig(
             num_layers=cfg.num_layers, hidden=cfg.hidden, intermediate=cfg.intermediate,
