@@ -76,6 +76,16 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
             rope_sin=pw.rope_sin.data_ptr())
         _lib.check(self.lib.mk_load_weights(self._handle, ctypes.byref(self._weights)))
 
+    @classmethod
+    def from_pretrained(cls, path, **kw) -> "MegakernelLlamaForCausalLM":
+        """Build from an HF checkpoint directory (config.json + safetensors), the
+        way the reference loads its model (llama.py:1287-1288); ``kw`` as for
+        the constructor."""
+        from .loader import load_hf_checkpoint
+
+        cfg, sd = load_hf_checkpoint(path)
+        return cls(cfg, sd, **kw)
+
     # ------------------------------------------------------------------ misc
     def __del__(self):
         h = self.__dict__.get("_handle")
@@ -193,6 +203,18 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
                             self._next[:B].to(torch.int64), kv)
 
     @torch.no_grad()
+    def prefill(self, input_ids: torch.Tensor,
+                past_key_values: PagedKVCache | None = None) -> DecodeOutput:
+        """Prompt prefill with PyTorch on the GPU (all positions of a layer at
+        once, see ``prefill.py``): fills the cache from each sequence's current
+        length and returns the last position's logits and greedy ids."""
+        from .prefill import prefill as _prefill
+
+        kv = past_key_values if past_key_values is not None else self.kv
+        logits, ids = _prefill(self, input_ids, kv)
+        return DecodeOutput(logits, ids, kv)
+
+    @torch.no_grad()
     def forward_hidden(self, hidden: torch.Tensor, position_ids: torch.Tensor,
                        past_key_values: PagedKVCache | None = None) -> torch.Tensor:
         """The decoder layers only (the reference kernel's X -> Y): [B, H] -> [B, H]."""
@@ -212,10 +234,13 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
 
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int,
-                 past_key_values: PagedKVCache | None = None) -> torch.Tensor:
+                 past_key_values: PagedKVCache | None = None,
+                 prefill: bool = False) -> torch.Tensor:
         """Greedy decoding: feed the prompt, then ``max_new_tokens`` steps on device.
 
-        The prompt goes through the decode kernel one position per launch.
+        The prompt goes through the decode kernel one position per launch, or
+        with ``prefill=True`` through the PyTorch prefill (all positions of a
+        layer at once; ``prefill.py``).
         The generated steps run back to back without host round trips: each
         launch writes its argmax into the next launch's token slot and bumps
         the position (MK_FLAG_FEEDBACK). Returns [B, max_new_tokens] int64.
@@ -225,7 +250,10 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         if ids.dim() == 1:
             ids = ids[None, :]
         B, T = ids.shape
-        out = self.forward(ids, past_key_values=kv, return_logits=False, sync=True)
+        if prefill:
+            out = self.prefill(ids, past_key_values=kv)
+        else:
+            out = self.forward(ids, past_key_values=kv, return_logits=False, sync=True)
         start = torch.tensor(kv.seq_lens[:B], dtype=torch.int32)
         for b in range(B):
             kv.reserve(b, int(start[b]) + max_new_tokens)

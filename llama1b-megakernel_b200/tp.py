@@ -123,6 +123,14 @@ class TensorParallelLlamaForCausalLM(MegakernelLlamaForCausalLM):
             ctypes.memmove(arr[r].bytes, h, 64)
         _lib.check(self.lib.mk_tp_connect(self._handle, arr, None))
 
+    @classmethod
+    def from_pretrained(cls, path, group=None, **kw) -> "TensorParallelLlamaForCausalLM":
+        """This rank of ``group``, from an HF checkpoint directory."""
+        from .loader import load_hf_checkpoint
+
+        cfg, sd = load_hf_checkpoint(path)
+        return cls(cfg, sd, group=group, **kw)
+
     @torch.no_grad()
     def forward(self, input_ids, position_ids=None, past_key_values=None, return_logits: bool = True,
                 sync: bool = True) -> DecodeOutput:
