@@ -202,6 +202,30 @@ int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed
 /* Launch geometry chosen by mk_init: CTAs (one per SM) and ring slots per CTA. */
 int mk_query(const MkModel* m, int32_t* grid, int32_t* ring_slots, int32_t* smem_bytes);
 
+/* ---- Sampling after the lm_head -------------------------------------------
+ *
+ * Per-sequence knobs of the reference's generation (top_k, top_p, temperature:
+ * main.py:57-61, prepare_sampling_params main.py:197-205, sampled on device
+ * through NxDI's OnDeviceSamplingConfig, main.py:129-130). */
+typedef struct MkSampling {
+  int32_t top_k;      /* 1: greedy; <= 0 or > 1024: 1024 */
+  float top_p;        /* (0, 1] */
+  float temperature;  /* <= 0: greedy */
+} MkSampling;
+
+/* Draw one token per sequence from fp32 logits [batch][ld] (the first `vocab`
+ * columns): divide by the temperature, keep the top_k largest (ties: lowest
+ * index first), softmax, keep the smallest prefix whose mass reaches top_p,
+ * and draw with a uniform hashed from (seed, step, sequence). Asynchronous
+ * on `stream` (launch it after mk_decode wrote the logits). With tokens and
+ * positions (device, [batch]) the draw is also written to tokens and the
+ * position advanced, as MK_FLAG_FEEDBACK does for the greedy argmax.
+ * *error (device int) is set to 1 if a sequence had more than 1024 logits
+ * tied at its top_k threshold (its id is then -1). batch <= 64. */
+int mk_sample(const float* logits, int32_t batch, int32_t vocab, int64_t ld,
+              const MkSampling* params, uint64_t seed, uint64_t step, int32_t* out_ids,
+              int32_t* tokens, int32_t* positions, int32_t* error, void* stream);
+
 /* ---- Tensor parallelism (one decode step over `world` GPUs) --------------
  *
  * Each rank's handle is made with mk_init from the rank's LOCAL geometry:

@@ -24,7 +24,8 @@ STATUS_NAMES = {
 EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
-    "mk_query", "mk_schedule_gap", "mk_tp_setup", "mk_tp_connect", "mk_last_error", "mk_destroy",
+    "mk_query", "mk_schedule_gap", "mk_sample", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
+    "mk_destroy",
 )
 
 
@@ -52,6 +53,11 @@ class MkWeights(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in (
         "embed", "w_qkv", "w_o", "w_gate_up", "w_down", "norm_attn", "norm_mlp",
         "norm_final", "rope_cos", "rope_sin")]
+
+
+class MkSampling(ctypes.Structure):
+    _fields_ = [("top_k", ctypes.c_int32), ("top_p", ctypes.c_float),
+                ("temperature", ctypes.c_float)]
 
 
 class MkIpcHandle(ctypes.Structure):
@@ -89,6 +95,8 @@ def load() -> ctypes.CDLL:
     lib.mk_set_trace.argtypes = [VP, VP, ctypes.c_int64, P(ctypes.c_int64)]
     lib.mk_query.argtypes = [VP, P(I32), P(I32), P(I32)]
     lib.mk_schedule_gap.argtypes = [P(MkConfig), I32, I32, P(I32)]
+    lib.mk_sample.argtypes = [VP, I32, I32, ctypes.c_int64, P(MkSampling), ctypes.c_uint64,
+                              ctypes.c_uint64, VP, VP, VP, VP, VP]
     lib.mk_tp_setup.argtypes = [VP, I32, I32, I32, I32, P(MkIpcHandle), P(VP)]
     lib.mk_tp_connect.argtypes = [VP, P(MkIpcHandle), P(VP)]
     lib.mk_last_error.argtypes = []

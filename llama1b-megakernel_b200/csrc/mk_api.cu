@@ -18,6 +18,7 @@
 
 #include "../../include/mk.h"
 #include "mk_kernel.cuh"
+#include "mk_sample.cuh"
 
 namespace {
 
@@ -685,6 +686,37 @@ int mk_schedule_gap(const MkConfig* cfg, int32_t batch, int32_t grid, int32_t* g
 }
 
 const char* mk_last_error(void) { return g_last_error.c_str(); }
+
+int mk_sample(const float* logits, int32_t batch, int32_t vocab, int64_t ld,
+              const MkSampling* params, uint64_t seed, uint64_t step, int32_t* out_ids,
+              int32_t* tokens, int32_t* positions, int32_t* error, void* stream) {
+  if (!logits || !params || !out_ids || !error) return fail(MK_EINVAL, "NULL argument");
+  if (batch < 1 || batch > mk::kSampleMaxBatch)
+    return fail(MK_EINVAL, "batch %d outside [1, %d]", batch, mk::kSampleMaxBatch);
+  if (vocab < 1 || ld < vocab) return fail(MK_EINVAL, "vocab %d / ld %lld", vocab, (long long)ld);
+  if ((tokens == nullptr) != (positions == nullptr))
+    return fail(MK_EINVAL, "tokens and positions go together");
+  mk::SampleParams sp{};
+  sp.logits = logits;
+  sp.ld = ld;
+  sp.V = vocab;
+  for (int b = 0; b < batch; ++b) {
+    const MkSampling& q = params[b];
+    if (!(q.top_p > 0.f) || q.top_p > 1.f) return fail(MK_EINVAL, "top_p %g outside (0, 1]", q.top_p);
+    sp.top_k[b] = q.top_k;
+    sp.top_p[b] = q.top_p;
+    sp.temperature[b] = q.temperature;
+  }
+  sp.seed = seed;
+  sp.step = step;
+  sp.out = out_ids;
+  sp.tokens = tokens;
+  sp.positions = positions;
+  sp.error = error;
+  mk::sample_kernel<<<batch, mk::kSampleThreads, 0, static_cast<cudaStream_t>(stream)>>>(sp);
+  MK_CUDA(cudaGetLastError());
+  return MK_OK;
+}
 
 int mk_tp_setup(MkModel* m, int32_t rank, int32_t world, int32_t lm_row0, int32_t lm_rows,
                 MkIpcHandle* handle, void** buffer) {

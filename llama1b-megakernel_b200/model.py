@@ -202,6 +202,28 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         return DecodeOutput(logits.clone() if logits is not None else None,
                             self._next[:B].to(torch.int64), kv)
 
+    def sample(self, logits: torch.Tensor, top_k: int = 1, top_p: float = 1.0,
+               temperature: float = 1.0, seed: int = 0, step: int = 0,
+               tokens: torch.Tensor | None = None, positions: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Draw one id per row of fp32 ``logits`` [B, V] on the device (``mk_sample``:
+        temperature, top_k, top_p, a uniform hashed from seed/step/row). With
+        ``tokens``/``positions`` the draw is fed back like MK_FLAG_FEEDBACK.
+        Asynchronous; returns the int32 ids tensor."""
+        B = logits.shape[0]
+        if out is None:
+            out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        if not hasattr(self, "_sample_err"):
+            self._sample_err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        params = (_lib.MkSampling * B)(*[_lib.MkSampling(int(top_k), float(top_p), float(temperature))
+                                          for _ in range(B)])
+        _lib.check(self.lib.mk_sample(
+            logits.data_ptr(), B, logits.shape[1], logits.stride(0), params, int(seed), int(step),
+            out.data_ptr(), tokens.data_ptr() if tokens is not None else None,
+            positions.data_ptr() if positions is not None else None, self._sample_err.data_ptr(),
+            self._stream_ptr(stream)))
+        return out
+
     @torch.no_grad()
     def prefill(self, input_ids: torch.Tensor,
                 past_key_values: PagedKVCache | None = None) -> DecodeOutput:
@@ -235,7 +257,8 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int,
                  past_key_values: PagedKVCache | None = None,
-                 prefill: bool = False) -> torch.Tensor:
+                 prefill: bool = False, do_sample: bool = False, top_k: int = 1,
+                 top_p: float = 1.0, temperature: float = 1.0, seed: int = 0) -> torch.Tensor:
         """Greedy decoding: feed the prompt, then ``max_new_tokens`` steps on device.
 
         The prompt goes through the decode kernel one position per launch, or
@@ -243,9 +266,15 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         layer at once; ``prefill.py``).
         The generated steps run back to back without host round trips: each
         launch writes its argmax into the next launch's token slot and bumps
-        the position (MK_FLAG_FEEDBACK). Returns [B, max_new_tokens] int64.
+        the position (MK_FLAG_FEEDBACK), or with ``do_sample`` each launch
+        writes its logits and ``mk_sample`` (``sample``) draws the next token
+        with ``top_k`` / ``top_p`` / ``temperature`` (draw s of the call uses
+        step s of ``seed``) and feeds it back the same way. Returns
+        [B, max_new_tokens] int64.
         """
         kv = past_key_values if past_key_values is not None else self.kv
+        if do_sample and self.lm_rows != self.cfg.vocab:
+            raise NotImplementedError("sampling needs the whole vocabulary's logits on one GPU")
         ids = torch.as_tensor(input_ids)
         if ids.dim() == 1:
             ids = ids[None, :]
@@ -253,21 +282,34 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         if prefill:
             out = self.prefill(ids, past_key_values=kv)
         else:
-            out = self.forward(ids, past_key_values=kv, return_logits=False, sync=True)
+            out = self.forward(ids, past_key_values=kv, return_logits=do_sample, sync=True)
         start = torch.tensor(kv.seq_lens[:B], dtype=torch.int32)
         for b in range(B):
             kv.reserve(b, int(start[b]) + max_new_tokens)
         tok = self._tokens[:B]
         pos = self._positions[:B]
-        tok.copy_(out.next_ids.to(torch.int32))
+        knobs = dict(top_k=top_k, top_p=top_p, temperature=temperature, seed=seed)
+        if do_sample:
+            self.sample(out.logits.to(self.device).contiguous(), step=0, out=tok, **knobs)
+        else:
+            tok.copy_(out.next_ids.to(torch.int32))
         pos.copy_(start.to(self.device))
         result = torch.empty(B, max_new_tokens, dtype=torch.int32, device=self.device)
         result[:, 0] = tok
+        logits = self._logits[:B]
         for s in range(1, max_new_tokens):
-            self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
+            if do_sample:
+                self.launch(tok, pos, kv, logits, self._next[:B])
+                self.sample(logits, step=s, tokens=tok, positions=pos, out=self._next[:B], **knobs)
+            else:
+                self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
             result[:, s] = tok
         self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
         self.sync()
+        if do_sample and int(self._sample_err[0]):
+            self._sample_err.zero_()
+            raise _lib.MkError(_lib.MK_EDEVICE, "sampling: more than 1024 logits tied at the top_k "
+                               "threshold")
         for b in range(B):
             kv.seq_lens[b] = int(start[b]) + max_new_tokens
         return result.to(torch.int64)
