@@ -42,33 +42,40 @@ def _slots(kv: PagedKVCache, seq: int, positions: torch.Tensor):
 
 
 @torch.no_grad()
-def prefill(model, input_ids: torch.Tensor, past_key_values: PagedKVCache | None = None):
-    """Run ``input_ids`` [B, T] (B sequences, each continuing from its cached
-    length) through ``model`` (a ``MegakernelLlamaForCausalLM``); returns
-    (logits [B, V] fp32 of the last position, greedy ids [B] int64)."""
+def prefill(model, input_ids, past_key_values: PagedKVCache | None = None):
+    """Run ``input_ids`` — [B, T], or a list of B 1-D tensors of any lengths —
+    through ``model`` (a ``MegakernelLlamaForCausalLM``), sequence b continuing
+    from its cached length; returns (logits [B, V] fp32 of each sequence's
+    last position, greedy ids [B] int64)."""
     cfg, pw = model.cfg, model.packed
     if getattr(model, "tp_world", 1) != 1:
         raise NotImplementedError("prefill runs on a single-GPU model")
     kv = past_key_values if past_key_values is not None else model.kv
-    ids = torch.as_tensor(input_ids)
-    if ids.dim() == 1:
-        ids = ids[None, :]
-    B, T = ids.shape
+    if isinstance(input_ids, (list, tuple)):
+        rows = [torch.as_tensor(r).reshape(-1) for r in input_ids]
+    else:
+        ids = torch.as_tensor(input_ids)
+        rows = list(ids[None, :] if ids.dim() == 1 else ids)
+    B = len(rows)
+    if B > model.max_batch:
+        raise ValueError(f"batch {B} > max_batch {model.max_batch}")
     dev = model.device
     H, NQ, NKV, I = cfg.hidden, cfg.num_q_heads, cfg.num_kv_heads, cfg.intermediate
     nh = NQ + 2 * NKV
     starts = [kv.seq_lens[b] for b in range(B)]
-    for b in range(B):
-        kv.reserve(b, starts[b] + T)
-    ids = ids.to(dev)
     last = []
-    for b in range(B):  # sequences differ in cached length: one at a time
+    for b in range(B):  # sequences differ in length: one at a time
+        T = rows[b].numel()
+        if T == 0:
+            raise ValueError(f"sequence {b} has no tokens")
+        kv.reserve(b, starts[b] + T)
+        ids_b = rows[b].to(dev)
         pos = torch.arange(starts[b], starts[b] + T, device=dev)
         page, off = _slots(kv, b, pos.cpu())
         allpos = torch.arange(0, starts[b] + T)
         apage, aoff = _slots(kv, b, allpos)
         cos, sin = pw.rope_cos[pos], pw.rope_sin[pos]
-        x = pw.embed[ids[b]]  # [T, H]
+        x = pw.embed[ids_b]  # [T, H]
         causal = allpos.to(dev)[None, :] <= pos[:, None]  # [T, P]
         for l in range(cfg.num_layers):
             h = _rms(x, pw.norm_attn[l], cfg.rms_eps)
