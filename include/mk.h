@@ -226,6 +226,26 @@ int mk_sample(const float* logits, int32_t batch, int32_t vocab, int64_t ld,
               const MkSampling* params, uint64_t seed, uint64_t step, int32_t* out_ids,
               int32_t* tokens, int32_t* positions, int32_t* error, void* stream);
 
+/* ---- Batched decode attention ---------------------------------------------
+ *
+ * One layer's decode attention for `batch` sequences over the paged cache:
+ * q [batch][num_q_heads][64] bf16 (post-RoPE), k_pages / v_pages the layer's
+ * [num_pages][num_kv_heads][page_size][64] bf16 pools, block_tables
+ * [batch][max_blocks] and lengths [batch] (device int32; sequence b attends
+ * positions [0, lengths[b]), which must already hold the step's own K/V),
+ * max_len >= every length; out [batch][num_q_heads][64] bf16 = softmax(q K^T
+ * * scale) V per head, GQA group 4 (nki_kernels/attention.py:270-399 for one
+ * sequence). Split-K over 256-position pieces, merged in a second launch.
+ * *error (device) is set to 1 if a block table names a page outside the
+ * pool (that position is skipped). Used by the batched decode path. */
+int64_t mk_paged_attention_workspace(int32_t batch, int32_t num_kv_heads, int32_t max_len);
+int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
+                       const int32_t* block_tables, const int32_t* lengths, int32_t batch,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t page_size,
+                       int32_t max_blocks, int32_t num_pages, int32_t max_len, float scale,
+                       void* workspace, int64_t workspace_bytes, void* out, int32_t* error,
+                       void* stream);
+
 /* ---- Tensor parallelism (one decode step over `world` GPUs) --------------
  *
  * Each rank's handle is made with mk_init from the rank's LOCAL geometry:

@@ -24,7 +24,8 @@ STATUS_NAMES = {
 EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
-    "mk_query", "mk_schedule_gap", "mk_sample", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
+    "mk_query", "mk_schedule_gap", "mk_sample", "mk_paged_attention_workspace",
+    "mk_paged_attention", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
     "mk_destroy",
 )
 
@@ -97,13 +98,17 @@ def load() -> ctypes.CDLL:
     lib.mk_schedule_gap.argtypes = [P(MkConfig), I32, I32, P(I32)]
     lib.mk_sample.argtypes = [VP, I32, I32, ctypes.c_int64, P(MkSampling), ctypes.c_uint64,
                               ctypes.c_uint64, VP, VP, VP, VP, VP]
+    lib.mk_paged_attention_workspace.argtypes = [I32, I32, I32]
+    lib.mk_paged_attention_workspace.restype = ctypes.c_int64
+    lib.mk_paged_attention.argtypes = [VP, VP, VP, VP, VP, I32, I32, I32, I32, I32, I32, I32,
+                                       ctypes.c_float, VP, ctypes.c_int64, VP, VP, VP]
     lib.mk_tp_setup.argtypes = [VP, I32, I32, I32, I32, P(MkIpcHandle), P(VP)]
     lib.mk_tp_connect.argtypes = [VP, P(MkIpcHandle), P(VP)]
     lib.mk_last_error.argtypes = []
     lib.mk_last_error.restype = ctypes.c_char_p
     lib.mk_destroy.argtypes = [VP]
     for name in EXPORTED:
-        if name != "mk_last_error":
+        if name not in ("mk_last_error", "mk_paged_attention_workspace"):
             getattr(lib, name).restype = ctypes.c_int
     _lib = lib
     return lib

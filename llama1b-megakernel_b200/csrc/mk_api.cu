@@ -19,6 +19,7 @@
 #include "../../include/mk.h"
 #include "mk_kernel.cuh"
 #include "mk_sample.cuh"
+#include "mk_attn.cuh"
 
 namespace {
 
@@ -686,6 +687,54 @@ int mk_schedule_gap(const MkConfig* cfg, int32_t batch, int32_t grid, int32_t* g
 }
 
 const char* mk_last_error(void) { return g_last_error.c_str(); }
+
+int64_t mk_paged_attention_workspace(int32_t batch, int32_t num_kv_heads, int32_t max_len) {
+  if (batch < 1 || num_kv_heads < 1 || max_len < 1) return 0;
+  const int64_t splits = (max_len + mk::kAttnSplitLen - 1) / mk::kAttnSplitLen;
+  return (int64_t)batch * num_kv_heads * splits * 4 * mk::kAttnPartial * 4;
+}
+
+int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
+                       const int32_t* block_tables, const int32_t* lengths, int32_t batch,
+                       int32_t num_q_heads, int32_t num_kv_heads, int32_t page_size,
+                       int32_t max_blocks, int32_t num_pages, int32_t max_len, float scale,
+                       void* workspace, int64_t workspace_bytes, void* out, int32_t* error,
+                       void* stream) {
+  if (!q || !k_pages || !v_pages || !block_tables || !lengths || !workspace || !out || !error)
+    return fail(MK_EINVAL, "NULL argument");
+  if (num_kv_heads < 1 || num_q_heads != 4 * num_kv_heads)
+    return fail(MK_EINVAL, "num_q_heads must be 4 * num_kv_heads");
+  if (batch < 1 || batch > 65535) return fail(MK_EINVAL, "batch %d", batch);
+  if (page_size < 1 || max_blocks < 1 || num_pages < 1 || max_len < 1 || max_len > page_size * max_blocks)
+    return fail(MK_EINVAL, "cache geometry (page_size %d, max_blocks %d, max_len %d)", page_size,
+                max_blocks, max_len);
+  if (!aligned16(q) || !aligned16(k_pages) || !aligned16(v_pages))
+    return fail(MK_EINVAL, "q and the page pools must be 16-byte aligned");
+  const int64_t need = mk_paged_attention_workspace(batch, num_kv_heads, max_len);
+  if (workspace_bytes < need) return fail(MK_EINVAL, "workspace %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
+  mk::PagedAttnParams ap{};
+  ap.q = static_cast<const mk::bf16*>(q);
+  ap.k = static_cast<const mk::bf16*>(k_pages);
+  ap.v = static_cast<const mk::bf16*>(v_pages);
+  ap.block_tables = block_tables;
+  ap.lengths = lengths;
+  ap.NQ = num_q_heads;
+  ap.NKV = num_kv_heads;
+  ap.ps = page_size;
+  ap.max_blocks = max_blocks;
+  ap.num_pages = num_pages;
+  ap.splits = (max_len + mk::kAttnSplitLen - 1) / mk::kAttnSplitLen;
+  ap.scale = scale;
+  ap.work = static_cast<float*>(workspace);
+  ap.out = static_cast<mk::bf16*>(out);
+  ap.error = error;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  mk::paged_attn_kernel<<<dim3(ap.splits, num_kv_heads, batch), mk::kAttnCtaWarps * 32, 0, st>>>(ap);
+  MK_CUDA(cudaGetLastError());
+  mk::paged_attn_merge_kernel<<<dim3(num_kv_heads, batch), 256, 0, st>>>(ap);
+  MK_CUDA(cudaGetLastError());
+  return MK_OK;
+}
 
 int mk_sample(const float* logits, int32_t batch, int32_t vocab, int64_t ld,
               const MkSampling* params, uint64_t seed, uint64_t step, int32_t* out_ids,

@@ -1,0 +1,199 @@
+// Batched decode attention over the paged KV cache (GQA group of 4, head_dim 64).
+//
+// The reference's decode attention (nki_kernels/attention.py:270-399) for one
+// sequence: per kv head g, scores s = q_h . K[:len] / 8 for its 4 q heads,
+// softmax, o_h = P . V. The batched decode path (many
+// sequences of ~1024 cached positions) reads B x 2 KB x len of K/V per layer,
+// as much as the weights at bs 64, so this kernel is built to stream it:
+//
+//  * grid (splits, kv heads, sequences); CTA (s, g, b) covers positions
+//    [s * kAttnSplitLen, (s+1) * kAttnSplitLen) of sequence b for the 4 q
+//    heads of kv head g, 4 warps over 32-position chunks of it;
+//  * a 32-position chunk is read in the natural orientation of each product:
+//    for the scores lane (r, h) dots q head h (in registers) with the K rows
+//    of positions r, r+8, r+16, r+24 (four lanes share each row load); for
+//    P . V lane j owns dims 2j, 2j+1 of all 32 V rows, for the 4 heads (each
+//    load instruction reads one 128-byte row);
+//  * online softmax in fp32 per head; the CTA's warps are merged in shared
+//    memory, and the CTA writes one (m, l, o[64]) partial per head;
+//  * a merge kernel (one CTA per sequence and kv head) combines the splits and
+//    writes o as bf16, the rounding of the attention output the single-GPU
+//    kernel uses.
+// Positions index pages through the block table; a page id outside the pool
+// sets the error word and the position is skipped (never dereferenced).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace mk {
+
+constexpr int kAttnSplitLen = 256;  // positions per CTA
+constexpr int kAttnCtaWarps = 4;
+constexpr int kAttnPartial = 2 + 64;  // m, l, o[64]
+
+struct PagedAttnParams {
+  const __nv_bfloat16* q;      // [B][NQ][64]
+  const __nv_bfloat16* k;      // layer base: [num_pages][NKV][ps][64]
+  const __nv_bfloat16* v;
+  const int* block_tables;     // [B][max_blocks]
+  const int* lengths;          // [B]: positions [0, len) are attended
+  int NQ, NKV, ps, max_blocks, num_pages, splits;
+  float scale;
+  float* work;                 // [B][NKV][splits][4][kAttnPartial]
+  __nv_bfloat16* out;          // [B][NQ][64]
+  int* error;
+};
+
+__device__ __forceinline__ float2 bf2x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+__global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __grid_constant__ PagedAttnParams p) {
+  __shared__ float pw[kAttnCtaWarps][4][32];               // probabilities of a chunk
+  __shared__ float st[kAttnCtaWarps][4][kAttnPartial];     // per-warp states
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // scores: lane = (position r8 of each 8, head h); P . V: lane = dims 2 lane, 2 lane + 1
+  const int h = lane & 3, r8 = lane >> 2;
+  const int len = p.lengths[b];
+  const int p0 = s * kAttnSplitLen, p1 = min(len, p0 + kAttnSplitLen);
+  float q[64];
+  {
+    const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.NQ + g * 4 + h) * 64);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 u = __ldg(qp + c);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = bf2x2(w[e]);
+        q[c * 8 + 2 * e] = f.x * p.scale;
+        q[c * 8 + 2 * e + 1] = f.y * p.scale;
+      }
+    }
+  }
+  float m = -INFINITY, l = 0.f;  // head h's running max and sum (same in its 8 lanes)
+  float o[4][2];
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh) o[hh][0] = o[hh][1] = 0.f;
+  const int* table = p.block_tables + (size_t)b * p.max_blocks;
+  for (int c0 = p0 + warp * 32; c0 < p1; c0 += kAttnCtaWarps * 32) {
+    float sc[4];
+    float cm = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int pos = c0 + r * 8 + r8;
+      sc[r] = -INFINITY;
+      if (pos < p1) {
+        const int page = table[pos / p.ps];
+        if (page < 0 || page >= p.num_pages) {
+          atomicExch(p.error, 1);
+        } else {
+          const uint4* kp = reinterpret_cast<const uint4*>(
+              p.k + (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64);
+          float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 u = kp[c];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = bf2x2(w[e]);
+              a0 = fmaf(f.x, q[c * 8 + 2 * e], a0);
+              a1 = fmaf(f.y, q[c * 8 + 2 * e + 1], a1);
+            }
+          }
+          sc[r] = a0 + a1;
+        }
+      }
+      cm = fmaxf(cm, sc[r]);
+    }
+    // head h's max and sum over the chunk: its 8 lanes differ in lane bits 2..4
+#pragma unroll
+    for (int d = 4; d < 32; d <<= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, d));
+    const float mn = fmaxf(m, cm);
+    const float alpha = (mn == -INFINITY) ? 1.f : __expf(m - mn);
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float e = (sc[r] == -INFINITY) ? 0.f : __expf(sc[r] - mn);
+      pw[warp][h][r * 8 + r8] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int d = 4; d < 32; d <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    l = l * alpha + sum;
+    m = mn;
+    __syncwarp();
+    // ---- P . V
+#pragma unroll
+    for (int hh = 0; hh < 4; ++hh) {
+      const float a = __shfl_sync(0xffffffffu, alpha, hh);  // lane hh holds head hh
+      o[hh][0] *= a;
+      o[hh][1] *= a;
+    }
+    const int n = min(32, p1 - c0);
+    for (int j = 0; j < n; ++j) {
+      const int pj = c0 + j;
+      const int page = table[pj / p.ps];
+      if (page < 0 || page >= p.num_pages) continue;
+      const uint32_t vw = reinterpret_cast<const uint32_t*>(
+          p.v + (((size_t)page * p.NKV + g) * p.ps + pj % p.ps) * 64)[lane];
+      const float2 f = bf2x2(vw);
+#pragma unroll
+      for (int hh = 0; hh < 4; ++hh) {
+        const float pr = pw[warp][hh][j];
+        o[hh][0] = fmaf(pr, f.x, o[hh][0]);
+        o[hh][1] = fmaf(pr, f.y, o[hh][1]);
+      }
+    }
+    __syncwarp();
+  }
+  // ---- merge the warps, write the CTA's partial per head
+  if (lane < 4) {
+    st[warp][h][0] = m;
+    st[warp][h][1] = l;
+  }
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh) {
+    st[warp][hh][2 + 2 * lane] = o[hh][0];
+    st[warp][hh][3 + 2 * lane] = o[hh][1];
+  }
+  __syncthreads();
+  float* dst = p.work + ((((size_t)b * p.NKV + g) * p.splits + s) * 4) * kAttnPartial;
+  for (int i = threadIdx.x; i < 4 * 64; i += kAttnCtaWarps * 32) {
+    const int hh = i >> 6, d = i & 63;
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnCtaWarps; ++w) M = fmaxf(M, st[w][hh][0]);
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < kAttnCtaWarps; ++w) {
+      const float a = (st[w][hh][0] == -INFINITY) ? 0.f : __expf(st[w][hh][0] - M);
+      L += st[w][hh][1] * a;
+      O += st[w][hh][2 + d] * a;
+    }
+    if (d == 0) {
+      dst[hh * kAttnPartial + 0] = M;
+      dst[hh * kAttnPartial + 1] = L;
+    }
+    dst[hh * kAttnPartial + 2 + d] = O;
+  }
+}
+
+__global__ void __launch_bounds__(256) paged_attn_merge_kernel(const __grid_constant__ PagedAttnParams p) {
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int h = threadIdx.x >> 6, d = threadIdx.x & 63;
+  const float* src = p.work + (((size_t)b * p.NKV + g) * p.splits * 4) * kAttnPartial;
+  float M = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, src[(s * 4 + h) * kAttnPartial]);
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < p.splits; ++s) {
+    const float* q = src + (s * 4 + h) * kAttnPartial;
+    const float a = (q[0] == -INFINITY) ? 0.f : __expf(q[0] - M);
+    L += q[1] * a;
+    O += q[2 + d] * a;
+  }
+  p.out[((size_t)b * p.NQ + g * 4 + h) * 64 + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+}
+
+}  // namespace mk

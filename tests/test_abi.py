@@ -22,7 +22,7 @@ def lib():
 
 def declared_symbols():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(mk_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(mk_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_header_declares_the_bound_symbols():
