@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--no-sweep", action="store_true", help="skip the ctx sweep extra")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the bs 8/32/64 extra")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a few steps, no e2e / sweep / cpu baseline")
@@ -388,6 +389,11 @@ def run_ours(args, ws, rank, local):
             del kv3
             torch.cuda.empty_cache()
 
+    # ------------------------------------------------------------ batched (config 4)
+    batched_res = None
+    if sweep and not args.no_batched:
+        batched_res = run_batched(model, cfg, dev, hbm_peak)
+
     # ------------------------------------------------------------ cpu baseline
     cpu_b = None
     if w_cpu is not None:
@@ -424,9 +430,49 @@ def run_ours(args, ws, rank, local):
         }
         if sweep_res is not None:
             line["ctx_sweep"] = sweep_res
+        if batched_res is not None:
+            line["batched"] = batched_res
         if cpu_b is not None:
             line["cpu_baseline"] = cpu_b
         print(json.dumps(line), flush=True)
+
+
+def run_batched(model, cfg, dev, hbm_peak):
+    """bs 8, 32, 64, one greedy step at KV length 1024 per
+    sequence (independent seeded N(0,1) caches, random tokens), through the
+    batched path (batched.py: paged attention kernel + cuBLAS projections, one
+    CUDA graph per batch size). Step time = median of 20 graph replays."""
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.batched import BatchedDecoder
+
+    L, BMAX = 1024, 64
+    dec = BatchedDecoder(model, max_batch=BMAX, max_seq_len=L + 64, page_size=64)
+    for b in range(BMAX):
+        k, v = syn.random_kv_rows(cfg, L, seed=100 + b, seq=b, device=dev)
+        dec.kv.fill(b, k, v)
+        del k, v
+    res = {}
+    for B in (8, 32, 64):
+        toks = syn.random_tokens(B, cfg.vocab, seed=B)
+        dec.step(toks, torch.full((B,), L, dtype=torch.int32))
+        for _ in range(3):
+            dec.replay(B)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(21)]
+        ev[0].record()
+        for j in range(20):
+            dec.replay(B)
+            ev[j + 1].record()
+        torch.cuda.synchronize()
+        dec.check()
+        med = statistics.median(ev[j].elapsed_time(ev[j + 1]) for j in range(20))
+        byts = cfg.weight_bytes_per_token() + B * cfg.kv_bytes_per_position() * (L + 1)
+        res[str(B)] = {"ms_p50": med, "tok_s": B * 1e3 / med, "bytes_per_step": byts,
+                       "achieved_gbs": byts / (med / 1e3) / 1e9,
+                       "frac_of_peak": byts / (med / 1e3) / 1e9 / hbm_peak,
+                       "gemm": "cuBLAS (torch F.linear)", "attention": "mk_paged_attention"}
+    del dec
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_case_small4():

@@ -246,6 +246,26 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
                        void* workspace, int64_t workspace_bytes, void* out, int32_t* error,
                        void* stream);
 
+/* Fused elementwise steps of the batched decode path, HF rounding (bf16 with
+ * fp32 statistics), asynchronous on `stream`:
+ * mk_rmsnorm_rows: out[r] = bf16(bf16(x[r] / sqrt(mean(x[r]^2) + eps)) * gamma)
+ *   for `rows` rows of `hidden` bf16 (llama.py:94-145 / HF LlamaRMSNorm);
+ * mk_rope_scatter: from qkv [batch][(nq + 2 nkv) * 64], the q/k/v GEMM output
+ *   in the packed RoPE-pair order, write q [batch][nq][64] and the K/V rows
+ *   into the layer's page pools at positions[b], RoPE (llama3 tables) on q and
+ *   k (attention.py:95-245 and the KV scatter, attention.py:450-492); a page id
+ *   outside the pool sets *error and the row is not written;
+ * mk_swiglu: out[i] = bf16(bf16(silu(g_i)) * u_i) from interleaved (g_i, u_i)
+ *   pairs, the packed w_gate_up order (mlp.py:60-192). */
+int mk_rmsnorm_rows(const void* x, const void* gamma, float eps, int32_t rows, int32_t hidden,
+                    void* out, void* stream);
+int mk_rope_scatter(const void* qkv, const void* rope_cos, const void* rope_sin,
+                    const int32_t* positions, const int32_t* block_tables, int32_t max_blocks,
+                    int32_t num_pages, int32_t page_size, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t batch, void* q_out, void* k_pages,
+                    void* v_pages, int32_t* error, void* stream);
+int mk_swiglu(const void* gate_up, int64_t n, void* out, void* stream);
+
 /* ---- Tensor parallelism (one decode step over `world` GPUs) --------------
  *
  * Each rank's handle is made with mk_init from the rank's LOCAL geometry:

@@ -6,19 +6,24 @@ skinny GEMMs ([B, K] x [K, N]) that CUDA cores cannot keep up with, and the
 KV cache (B x 2 KB x 1024 per layer) is read as much as the weights. This
 path runs one step as:
 
-* per layer: RMSNorm, the q/k/v GEMM on the packed ``w_qkv`` (the RoPE-pair
-  order undone on the output), RoPE, the K/V rows scattered into the paged
-  cache, attention by this library's paged split-K decode kernel
-  (``mk_paged_attention``, csrc/mk_attn.cuh: the HBM-heavy part), o_proj and
-  the SwiGLU MLP as GEMMs; then the final norm, lm_head and argmax;
-* the GEMMs are cuBLAS (tensor cores) through ``torch.nn.functional.linear``
-  on the kernel's own packed weights; the elementwise steps are torch ops;
+* per layer: RMSNorm (``mk_rmsnorm_rows``), the q/k/v GEMM on the packed
+  ``w_qkv``, RoPE with the K/V rows scattered into the paged cache
+  (``mk_rope_scatter``, which reads the RoPE-pair column order directly),
+  attention by this library's paged split-K decode kernel
+  (``mk_paged_attention``, csrc/mk_attn.cuh: the HBM-heavy part), o_proj with
+  the residual added by the GEMM (``addmm``), RMSNorm, the gate/up GEMM,
+  ``mk_swiglu``, down with the residual; then the final norm, lm_head and
+  argmax;
+* the GEMMs are cuBLAS (tensor cores) through torch on the kernel's own packed
+  weights; the elementwise steps are this library's fused kernels
+  (csrc/mk_batched.cuh);
 * the whole step is captured once per batch size into a CUDA graph, so a step
   is one graph launch with the tokens and positions on the device.
 
-Rounding follows HF's decode step in bf16 (as the prefill path does), and the
-attention output is rounded to bf16 from fp32 softmax sums (as the megakernel
-does).
+Rounding follows HF's decode step in bf16 (as the prefill path does), except
+that a residual add happens inside the GEMM's fp32 epilogue (one bf16
+rounding of x + W a instead of two); the attention output is rounded to bf16
+from fp32 softmax sums (as the megakernel does).
 """
 from __future__ import annotations
 
@@ -29,14 +34,6 @@ import torch.nn.functional as F
 
 from . import _lib
 from .kv_cache import PagedKVCache
-from .prefill import _rms
-
-
-def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """HF ``apply_rotary_pos_emb`` on [B, heads, 64] with [B, 64] tables."""
-    half = x.shape[-1] // 2
-    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
-    return x * cos[:, None, :] + rot * sin[:, None, :]
 
 
 class BatchedDecoder:
@@ -47,6 +44,9 @@ class BatchedDecoder:
                  num_pages: int | None = None):
         if getattr(model, "tp_world", 1) != 1:
             raise NotImplementedError("the batched path runs on one GPU")
+        if max_seq_len > model.rope_len:
+            raise ValueError(f"max_seq_len {max_seq_len} exceeds the model's RoPE table "
+                             f"({model.rope_len} positions)")
         self.m = model
         self.cfg = model.cfg
         self.dev = model.device
@@ -71,30 +71,36 @@ class BatchedDecoder:
             out.data_ptr(), self.err.data_ptr(), torch.cuda.current_stream().cuda_stream))
 
     def _step(self, tokens, positions, logits_out, ids_out):
-        c, pw, kv = self.cfg, self.m.packed, self.kv
+        c, pw, kv, lib = self.cfg, self.m.packed, self.kv, self.lib
         B = tokens.numel()
         H, NQ, NKV, I = c.hidden, c.num_q_heads, c.num_kv_heads, c.intermediate
-        nh = NQ + 2 * NKV
-        pos = positions.long()
+        st = torch.cuda.current_stream().cuda_stream
+        dev = self.dev
         x = pw.embed[tokens.long()]
-        cos, sin = pw.rope_cos[pos], pw.rope_sin[pos]
-        page = kv.block_tables[:B].gather(1, (pos // kv.page_size)[:, None])[:, 0].long()
-        off = pos % kv.page_size
         lengths = (positions + 1).to(torch.int32)
-        attn = torch.empty(B, NQ, 64, dtype=torch.bfloat16, device=self.dev)
+        h = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+        q = torch.empty(B, NQ, 64, dtype=torch.bfloat16, device=dev)
+        attn = torch.empty(B, NQ, 64, dtype=torch.bfloat16, device=dev)
+        act = torch.empty(B, I, dtype=torch.bfloat16, device=dev)
         for l in range(c.num_layers):
-            h = _rms(x, pw.norm_attn[l], c.rms_eps)
-            qkv = F.linear(h, pw.w_qkv[l].view(-1, H)).view(B, nh, 32, 2).transpose(-1, -2)
-            qkv = qkv.reshape(B, nh, 64)
-            q = _rope(qkv[:, :NQ], cos, sin).contiguous()
-            kv.k_pages[l, page, :, off] = _rope(qkv[:, NQ:NQ + NKV], cos, sin)
-            kv.v_pages[l, page, :, off] = qkv[:, NQ + NKV:]
+            _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_attn[l].data_ptr(),
+                                           ctypes.c_float(c.rms_eps), B, H, h.data_ptr(), st))
+            qkv = F.linear(h, pw.w_qkv[l].view(-1, H))  # packed RoPE-pair column order
+            _lib.check(lib.mk_rope_scatter(
+                qkv.data_ptr(), pw.rope_cos.data_ptr(), pw.rope_sin.data_ptr(),
+                positions.data_ptr(), kv.block_tables.data_ptr(), kv.max_blocks, kv.num_pages,
+                kv.page_size, NQ, NKV, B, q.data_ptr(), kv.k_pages[l].data_ptr(),
+                kv.v_pages[l].data_ptr(), self.err.data_ptr(), st))
             self._attention(q, l, lengths, B, attn)
-            x = x + F.linear(attn.view(B, NQ * 64), pw.w_o[l])
-            h = _rms(x, pw.norm_mlp[l], c.rms_eps)
-            gu = F.linear(h, pw.w_gate_up[l].view(2 * I, H)).view(B, I, 2)
-            x = x + F.linear(F.silu(gu[..., 0]) * gu[..., 1], pw.w_down[l])
-        lg = F.linear(_rms(x, pw.norm_final, c.rms_eps), pw.embed)
+            x = torch.addmm(x, attn.view(B, NQ * 64), pw.w_o[l].t())  # residual in the GEMM
+            _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_mlp[l].data_ptr(),
+                                           ctypes.c_float(c.rms_eps), B, H, h.data_ptr(), st))
+            gu = F.linear(h, pw.w_gate_up[l].view(2 * I, H))  # (gate, up) interleaved
+            _lib.check(lib.mk_swiglu(gu.data_ptr(), B * I, act.data_ptr(), st))
+            x = torch.addmm(x, act, pw.w_down[l].t())
+        _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_final.data_ptr(),
+                                       ctypes.c_float(c.rms_eps), B, H, h.data_ptr(), st))
+        lg = F.linear(h, pw.embed)
         logits_out.copy_(lg)
         ids_out.copy_(lg.argmax(dim=-1))
 
@@ -137,6 +143,8 @@ class BatchedDecoder:
         if B > self.max_batch:
             raise ValueError(f"batch {B} > {self.max_batch}")
         pos_host = torch.as_tensor(positions).cpu()
+        if bool((pos_host < 0).any()) or bool((pos_host >= self.max_seq_len).any()):
+            raise ValueError(f"positions must be in [0, {self.max_seq_len})")
         for b in range(B):
             self.kv.reserve(b, int(pos_host[b]) + 1)
         graph, tok, pos, logits, ids = self._graph(B)

@@ -20,6 +20,7 @@
 #include "mk_kernel.cuh"
 #include "mk_sample.cuh"
 #include "mk_attn.cuh"
+#include "mk_batched.cuh"
 
 namespace {
 
@@ -732,6 +733,46 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
   mk::paged_attn_kernel<<<dim3(ap.splits, num_kv_heads, batch), mk::kAttnCtaWarps * 32, 0, st>>>(ap);
   MK_CUDA(cudaGetLastError());
   mk::paged_attn_merge_kernel<<<dim3(num_kv_heads, batch), 256, 0, st>>>(ap);
+  MK_CUDA(cudaGetLastError());
+  return MK_OK;
+}
+
+int mk_rmsnorm_rows(const void* x, const void* gamma, float eps, int32_t rows, int32_t hidden,
+                    void* out, void* stream) {
+  if (!x || !gamma || !out) return fail(MK_EINVAL, "NULL argument");
+  if (rows < 1 || hidden < 8 || hidden % 8) return fail(MK_EINVAL, "rows %d, hidden %d", rows, hidden);
+  if (!aligned16(x) || !aligned16(gamma) || !aligned16(out)) return fail(MK_EINVAL, "16-byte alignment");
+  mk::rmsnorm_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const mk::bf16*>(x), static_cast<const mk::bf16*>(gamma), eps, hidden,
+      static_cast<mk::bf16*>(out));
+  MK_CUDA(cudaGetLastError());
+  return MK_OK;
+}
+
+int mk_rope_scatter(const void* qkv, const void* rope_cos, const void* rope_sin,
+                    const int32_t* positions, const int32_t* block_tables, int32_t max_blocks,
+                    int32_t num_pages, int32_t page_size, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t batch, void* q_out, void* k_pages,
+                    void* v_pages, int32_t* error, void* stream) {
+  if (!qkv || !rope_cos || !rope_sin || !positions || !block_tables || !q_out || !k_pages ||
+      !v_pages || !error)
+    return fail(MK_EINVAL, "NULL argument");
+  if (batch < 1 || num_q_heads < 1 || num_kv_heads < 1 || page_size < 1 || max_blocks < 1)
+    return fail(MK_EINVAL, "geometry");
+  const int n = batch * (num_q_heads + 2 * num_kv_heads) * 32;
+  mk::rope_scatter_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const mk::bf16*>(qkv), static_cast<const mk::bf16*>(rope_cos),
+      static_cast<const mk::bf16*>(rope_sin), positions, block_tables, max_blocks, num_pages,
+      page_size, num_q_heads, num_kv_heads, batch, static_cast<mk::bf16*>(q_out),
+      static_cast<mk::bf16*>(k_pages), static_cast<mk::bf16*>(v_pages), error);
+  MK_CUDA(cudaGetLastError());
+  return MK_OK;
+}
+
+int mk_swiglu(const void* gate_up, int64_t n, void* out, void* stream) {
+  if (!gate_up || !out || n < 1 || n > INT32_MAX) return fail(MK_EINVAL, "arguments");
+  mk::swiglu_kernel<<<(int)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const mk::bf16*>(gate_up), (int)n, static_cast<mk::bf16*>(out));
   MK_CUDA(cudaGetLastError());
   return MK_OK;
 }

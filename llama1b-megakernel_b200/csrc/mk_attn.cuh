@@ -11,9 +11,10 @@
 //    heads of kv head g, 4 warps over 32-position chunks of it;
 //  * a 32-position chunk is read in the natural orientation of each product:
 //    for the scores lane (r, h) dots q head h (in registers) with the K rows
-//    of positions r, r+8, r+16, r+24 (four lanes share each row load); for
-//    P . V lane j owns dims 2j, 2j+1 of all 32 V rows, for the 4 heads (each
-//    load instruction reads one 128-byte row);
+//    of positions r, r+8, r+16, r+24 (four lanes share each row load); the V
+//    rows go through shared memory (8 independent 16-byte loads per lane,
+//    issued before the scores) and for P . V lane j owns dims 2j, 2j+1 of all
+//    32 rows, for the 4 heads;
 //  * online softmax in fp32 per head; the CTA's warps are merged in shared
 //    memory, and the CTA writes one (m, l, o[64]) partial per head;
 //  * a merge kernel (one CTA per sequence and kv head) combines the splits and
@@ -28,7 +29,7 @@
 
 namespace mk {
 
-constexpr int kAttnSplitLen = 256;  // positions per CTA
+constexpr int kAttnSplitLen = 128;  // positions per CTA
 constexpr int kAttnCtaWarps = 4;
 constexpr int kAttnPartial = 2 + 64;  // m, l, o[64]
 
@@ -51,6 +52,7 @@ __device__ __forceinline__ float2 bf2x2(uint32_t w) {
 
 __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __grid_constant__ PagedAttnParams p) {
   __shared__ float pw[kAttnCtaWarps][4][32];               // probabilities of a chunk
+  __shared__ uint4 vbuf[kAttnCtaWarps][32][8];             // a chunk's V rows
   __shared__ float st[kAttnCtaWarps][4][kAttnPartial];     // per-warp states
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -79,34 +81,60 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
   for (int hh = 0; hh < 4; ++hh) o[hh][0] = o[hh][1] = 0.f;
   const int* table = p.block_tables + (size_t)b * p.max_blocks;
   for (int c0 = p0 + warp * 32; c0 < p1; c0 += kAttnCtaWarps * 32) {
-    float sc[4];
-    float cm = -INFINITY;
+    // V rows of the chunk into shared memory: 8 independent 16-byte loads per
+    // lane, 4 rows per load instruction (rows past the end or in a bad page: 0)
+    {
+      uint4 t[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int row = k * 4 + (lane >> 3), pos = c0 + row;
+        t[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (pos < p1) {
+          const int page = table[pos / p.ps];
+          if (page >= 0 && page < p.num_pages)
+            t[k] = reinterpret_cast<const uint4*>(
+                p.v + (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64)[lane & 7];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) vbuf[warp][k * 4 + (lane >> 3)][lane & 7] = t[k];
+    }
+    // scores: addresses of the 4 positions first, then all 32 loads
+    const uint4* kp[4];
+    bool kok[4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int pos = c0 + r * 8 + r8;
-      sc[r] = -INFINITY;
+      kok[r] = false;
+      kp[r] = reinterpret_cast<const uint4*>(p.k);
       if (pos < p1) {
         const int page = table[pos / p.ps];
         if (page < 0 || page >= p.num_pages) {
           atomicExch(p.error, 1);
         } else {
-          const uint4* kp = reinterpret_cast<const uint4*>(
+          kok[r] = true;
+          kp[r] = reinterpret_cast<const uint4*>(
               p.k + (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64);
-          float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint4 u = kp[c];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = bf2x2(w[e]);
-              a0 = fmaf(f.x, q[c * 8 + 2 * e], a0);
-              a1 = fmaf(f.y, q[c * 8 + 2 * e + 1], a1);
-            }
-          }
-          sc[r] = a0 + a1;
         }
       }
+    }
+    float sc[4];
+    float cm = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 u = kok[r] ? kp[r][c] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = bf2x2(w[e]);
+          a0 = fmaf(f.x, q[c * 8 + 2 * e], a0);
+          a1 = fmaf(f.y, q[c * 8 + 2 * e + 1], a1);
+        }
+      }
+      sc[r] = kok[r] ? a0 + a1 : -INFINITY;
       cm = fmaxf(cm, sc[r]);
     }
     // head h's max and sum over the chunk: its 8 lanes differ in lane bits 2..4
@@ -135,11 +163,7 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
     }
     const int n = min(32, p1 - c0);
     for (int j = 0; j < n; ++j) {
-      const int pj = c0 + j;
-      const int page = table[pj / p.ps];
-      if (page < 0 || page >= p.num_pages) continue;
-      const uint32_t vw = reinterpret_cast<const uint32_t*>(
-          p.v + (((size_t)page * p.NKV + g) * p.ps + pj % p.ps) * 64)[lane];
+      const uint32_t vw = reinterpret_cast<const uint32_t*>(&vbuf[warp][j][0])[lane];
       const float2 f = bf2x2(vw);
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {

@@ -1,0 +1,115 @@
+// Fused elementwise steps of the batched decode path (batched.py).
+//
+// Between the projections of a batched step, HF's decode layer does RMSNorm,
+// RoPE on q and k, the K/V cache write, and SiLU(gate) * up, each a handful
+// of small tensor ops. These kernels do each step in one launch with HF's
+// rounding (the same formulas as the persistent kernel's epilogues):
+//   rmsnorm:  y = bf16(bf16(x * 1/sqrt(mean(x^2) + eps)) * gamma), sums in fp32
+//   rope:     y0 = bf16(bf16(x0 c0) + bf16(-x1 s0)), y1 = bf16(bf16(x1 c1) + bf16(x0 s1))
+//             for the pair (d, d + 32) of every q and k head, from the bf16
+//             cos/sin table rows of the step's positions
+//   swiglu:   a = bf16(bf16(g / (1 + exp(-g))) * u)
+#pragma once
+
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace mk {
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// One CTA of 256 threads per row; H a multiple of 8.
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const __nv_bfloat16* x, const __nv_bfloat16* gamma,
+                                                           float eps, int H, __nv_bfloat16* y) {
+  __shared__ float red[8];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)b * H);
+  float ss = 0.f;
+  for (int i = tid; i < H / 8; i += 256) {
+    const uint4 u = xr[i];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a = __uint_as_float(w[e] << 16), c = __uint_as_float(w[e] & 0xFFFF0000u);
+      ss = fmaf(a, a, ss);
+      ss = fmaf(c, c, ss);
+    }
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w];
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), eps)));
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)b * H);
+  for (int i = tid; i < H / 8; i += 256) {
+    const uint4 u = xr[i], g = gr[i];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w}, gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bfr(bfr(__uint_as_float(w[e] << 16) * r) * __uint_as_float(gw[e] << 16));
+      const float hi = bfr(bfr(__uint_as_float(w[e] & 0xFFFF0000u) * r) * __uint_as_float(gw[e] & 0xFFFF0000u));
+      __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+      o[e] = *reinterpret_cast<uint32_t*>(&pr);
+    }
+    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// qkv: [B][(NQ + 2 NKV) * 64] GEMM output in the packed RoPE-pair order
+// (column head * 64 + 2 d + pair holds dim d + 32 pair of the head). Writes q
+// [B][NQ][64] (rotated) and the rotated k / plain v rows into the layer's page
+// pools at the step's positions. One thread per (sequence, head, d < 32).
+__global__ void __launch_bounds__(256) rope_scatter_kernel(
+    const __nv_bfloat16* qkv, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
+    const int* positions, const int* block_tables, int max_blocks, int num_pages, int ps, int NQ,
+    int NKV, int B, __nv_bfloat16* q_out, __nv_bfloat16* k_pages, __nv_bfloat16* v_pages, int* error) {
+  const int nh = NQ + 2 * NKV;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * nh * 32) return;
+  const int d = i & 31, hd = (i >> 5) % nh, b = (i >> 5) / nh;
+  const __nv_bfloat16* src = qkv + ((size_t)b * nh + hd) * 64 + 2 * d;
+  float x0 = __bfloat162float(src[0]), x1 = __bfloat162float(src[1]);
+  const int pos = positions[b];
+  if (hd < NQ + NKV) {
+    const __nv_bfloat16* cr = cos_t + (size_t)pos * 64;
+    const __nv_bfloat16* sr = sin_t + (size_t)pos * 64;
+    const float c0 = __bfloat162float(cr[d]), c1 = __bfloat162float(cr[d + 32]);
+    const float s0 = __bfloat162float(sr[d]), s1 = __bfloat162float(sr[d + 32]);
+    const float y0 = bfr(bfr(x0 * c0) + bfr(-x1 * s0));
+    const float y1 = bfr(bfr(x1 * c1) + bfr(x0 * s1));
+    x0 = y0;
+    x1 = y1;
+  }
+  if (hd < NQ) {
+    __nv_bfloat16* qr = q_out + ((size_t)b * NQ + hd) * 64;
+    qr[d] = __float2bfloat16_rn(x0);
+    qr[d + 32] = __float2bfloat16_rn(x1);
+    return;
+  }
+  const bool is_k = hd < NQ + NKV;
+  const int g = is_k ? hd - NQ : hd - NQ - NKV;
+  const int page = block_tables[(size_t)b * max_blocks + pos / ps];
+  if (page < 0 || page >= num_pages) {
+    atomicExch(error, 1);
+    return;
+  }
+  __nv_bfloat16* dst = (is_k ? k_pages : v_pages) + (((size_t)page * NKV + g) * ps + pos % ps) * 64;
+  dst[d] = __float2bfloat16_rn(x0);
+  dst[d + 32] = __float2bfloat16_rn(x1);
+}
+
+// gu: [B][I][2] (gate, up interleaved, the packed w_gate_up order) -> a [B][I].
+__global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* gu, int n, __nv_bfloat16* a) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const __nv_bfloat162 p = reinterpret_cast<const __nv_bfloat162*>(gu)[i];
+  const float g = __bfloat162float(p.x), u = __bfloat162float(p.y);
+  const float s = bfr(__fdiv_rn(g, 1.0f + expf(-g)));
+  a[i] = __float2bfloat16_rn(s * u);
+}
+
+}  // namespace mk

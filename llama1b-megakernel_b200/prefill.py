@@ -68,6 +68,9 @@ def prefill(model, input_ids, past_key_values: PagedKVCache | None = None):
         T = rows[b].numel()
         if T == 0:
             raise ValueError(f"sequence {b} has no tokens")
+        if starts[b] + T > pw.rope_cos.shape[0]:
+            raise ValueError(f"sequence {b}: positions up to {starts[b] + T - 1} exceed the RoPE "
+                             f"table ({pw.rope_cos.shape[0]} positions)")
         kv.reserve(b, starts[b] + T)
         ids_b = rows[b].to(dev)
         pos = torch.arange(starts[b], starts[b] + T, device=dev)

@@ -99,3 +99,16 @@ def test_bad_page_reported(setup):
     dec.step(syn.random_tokens(2, SMALL.vocab, seed=1), torch.tensor([300, 20]))
     with pytest.raises(Exception, match="outside the pool"):
         dec.check()
+
+
+def test_positions_beyond_rope_table_refused(setup):
+    _, m = setup  # RoPE table of 640 positions
+    with pytest.raises(ValueError, match="RoPE"):
+        BatchedDecoder(m, max_batch=2, max_seq_len=m.rope_len + 1)
+    dec = BatchedDecoder(m, max_batch=1, max_seq_len=m.rope_len)
+    with pytest.raises(ValueError):
+        dec.step(torch.tensor([1]), torch.tensor([m.rope_len]))
+    kv = m.new_cache(max_seq_len=m.rope_len + 64, num_pages=64)
+    kv.seq_lens[0] = m.rope_len - 2
+    with pytest.raises(ValueError, match="RoPE"):
+        m.prefill(torch.arange(5)[None], past_key_values=kv)
