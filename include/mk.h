@@ -246,6 +246,21 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
                        void* workspace, int64_t workspace_bytes, void* out, int32_t* error,
                        void* stream);
 
+/* Skinny GEMM on the tcgen05 tensor cores for the batched decode path:
+ * Y[rows][n] = X[rows][k] . W[n][k]^T (+ residual[rows][n]), bf16 inputs,
+ * fp32 accumulation, Y bf16 (out) or fp32 (out_f32, no residual). W is a
+ * weight matrix in HF [out][in] layout (n a multiple of 128, k of 64); X has
+ * rows_padded (16, 32 or 64) rows of which the first `rows` are real and the
+ * rest zero. Narrow W is split along k across CTAs; then `workspace` must
+ * hold mk_gemm_workspace(n, k, rows) bytes. *error (device) records a wait
+ * that ran out (the kernel's waits are time-bounded). Asynchronous. These
+ * are the projections of the reference's decoder (attention.py:95-245,
+ * :409-448, mlp.py:60-192, the lm_head llama.py:1208-1227) at batch > 1. */
+int64_t mk_gemm_workspace(int32_t n, int32_t k, int32_t rows);
+int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t rows,
+                 int32_t rows_padded, const void* residual, void* out, float* out_f32,
+                 void* workspace, int64_t workspace_bytes, int32_t* error, void* stream);
+
 /* Fused elementwise steps of the batched decode path, HF rounding (bf16 with
  * fp32 statistics), asynchronous on `stream`:
  * mk_rmsnorm_rows: out[r] = bf16(bf16(x[r] / sqrt(mean(x[r]^2) + eps)) * gamma)

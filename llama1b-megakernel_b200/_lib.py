@@ -25,7 +25,7 @@ EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_schedule_gap", "mk_sample", "mk_paged_attention_workspace",
-    "mk_paged_attention", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
+    "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
     "mk_destroy",
 )
 
@@ -102,6 +102,9 @@ def load() -> ctypes.CDLL:
     lib.mk_paged_attention_workspace.restype = ctypes.c_int64
     lib.mk_paged_attention.argtypes = [VP, VP, VP, VP, VP, I32, I32, I32, I32, I32, I32, I32,
                                        ctypes.c_float, VP, ctypes.c_int64, VP, VP, VP]
+    lib.mk_gemm_workspace.argtypes = [I32, I32, I32]
+    lib.mk_gemm_workspace.restype = ctypes.c_int64
+    lib.mk_gemm_bf16.argtypes = [VP, I32, I32, VP, I32, I32, VP, VP, VP, VP, ctypes.c_int64, VP, VP]
     lib.mk_rmsnorm_rows.argtypes = [VP, VP, ctypes.c_float, I32, I32, VP, VP]
     lib.mk_rope_scatter.argtypes = [VP, VP, VP, VP, VP, I32, I32, I32, I32, I32, I32, VP, VP, VP,
                                     VP, VP]
@@ -112,7 +115,7 @@ def load() -> ctypes.CDLL:
     lib.mk_last_error.restype = ctypes.c_char_p
     lib.mk_destroy.argtypes = [VP]
     for name in EXPORTED:
-        if name not in ("mk_last_error", "mk_paged_attention_workspace"):
+        if name not in ("mk_last_error", "mk_paged_attention_workspace", "mk_gemm_workspace"):
             getattr(lib, name).restype = ctypes.c_int
     _lib = lib
     return lib

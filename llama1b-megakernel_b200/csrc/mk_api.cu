@@ -21,6 +21,7 @@
 #include "mk_sample.cuh"
 #include "mk_attn.cuh"
 #include "mk_batched.cuh"
+#include "mk_gemm.cuh"
 
 namespace {
 
@@ -363,6 +364,58 @@ int static_setup(int device, void** out) {
   return MK_OK;
 }
 
+}  // namespace
+
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// A 2-D bf16 tensor map [rows][cols] (cols contiguous), box {64 cols, box_rows},
+// 128-byte swizzle: the K-major operand layout of the tcgen05 GEMM.
+int encode_sw128(CUtensorMap* out, const void* base, long long rows, long long cols, int box_rows) {
+  static EncodeTiledFn enc = nullptr;
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      return fail(MK_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    enc = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {(cuuint32_t)mk::kGemmTileK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MK_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MK_OK;
+}
+
+// K blocks per split for an n x k GEMM: narrow W is split along K so the
+// grid covers the SMs.
+int gemm_kblocks_per_split(int n, int k, int sms) {
+  const int tiles = n / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
+  int splits = tiles >= sms / 2 ? 1 : (sms + tiles - 1) / tiles;
+  if (splits > kblocks) splits = kblocks;
+  return (kblocks + splits - 1) / splits;
+}
+
+template <int BP>
+cudaError_t launch_gemm(const mk::GemmParams& gp, int tiles, int splits, cudaStream_t st) {
+  const int smem = mk::kGemmStages * (mk::kGemmTileN + BP) * mk::kGemmTileK * 2 + 1024;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(mk::gemm_kernel<BP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  mk::gemm_kernel<BP><<<dim3(tiles, splits), mk::kGemmThreads, smem, st>>>(gp);
+  return cudaGetLastError();
+}
 }  // namespace
 
 extern "C" {
@@ -734,6 +787,63 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
   MK_CUDA(cudaGetLastError());
   mk::paged_attn_merge_kernel<<<dim3(num_kv_heads, batch), 256, 0, st>>>(ap);
   MK_CUDA(cudaGetLastError());
+  return MK_OK;
+}
+
+int64_t mk_gemm_workspace(int32_t n, int32_t k, int32_t rows) {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (n < mk::kGemmTileN || k < mk::kGemmTileK || rows < 1) return 0;
+  const int kps = gemm_kblocks_per_split(n, k, sms);
+  const int splits = (k / mk::kGemmTileK + kps - 1) / kps;
+  return splits > 1 ? (int64_t)splits * rows * n * 4 : 0;
+}
+
+int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t rows,
+                 int32_t rows_padded, const void* residual, void* out, float* out_f32,
+                 void* workspace, int64_t workspace_bytes, int32_t* error, void* stream) {
+  if (!w || !x || !error || (!out && !out_f32) || (out && out_f32))
+    return fail(MK_EINVAL, "w, x, error and exactly one of out / out_f32 are required");
+  if (n < mk::kGemmTileN || n % mk::kGemmTileN || k < mk::kGemmTileK || k % mk::kGemmTileK)
+    return fail(MK_EINVAL, "n must be a multiple of 128 and k of 64 (n %d, k %d)", n, k);
+  if (rows_padded != 16 && rows_padded != 32 && rows_padded != 64)
+    return fail(MK_EINVAL, "rows_padded must be 16, 32 or 64 (got %d)", rows_padded);
+  if (rows < 1 || rows > rows_padded) return fail(MK_EINVAL, "rows %d outside [1, %d]", rows, rows_padded);
+  if (!aligned16(w) || !aligned16(x)) return fail(MK_EINVAL, "w and x must be 16-byte aligned");
+  if (residual && out_f32) return fail(MK_EINVAL, "a residual needs the bf16 output");
+  int dev = 0, sms = 148;
+  MK_CUDA(cudaGetDevice(&dev));
+  MK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int tiles = n / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
+  const int kps = gemm_kblocks_per_split(n, k, sms);
+  const int splits = (kblocks + kps - 1) / kps;
+  if (splits > 1 && (!workspace || workspace_bytes < (int64_t)splits * rows * n * 4))
+    return fail(MK_EINVAL, "split-K needs a workspace of %lld bytes", (long long)splits * rows * n * 4);
+  mk::GemmParams gp{};
+  if (int rc = encode_sw128(&gp.tm_w, w, n, k, mk::kGemmTileN)) return rc;
+  if (int rc = encode_sw128(&gp.tm_x, x, rows_padded, k, rows_padded)) return rc;
+  gp.N = n;
+  gp.K = k;
+  gp.B = rows;
+  gp.kblocks_per_split = kps;
+  gp.residual = splits > 1 ? nullptr : static_cast<const mk::bf16*>(residual);
+  gp.out = splits > 1 ? nullptr : static_cast<mk::bf16*>(out);
+  gp.out_f32 = splits > 1 ? nullptr : out_f32;
+  gp.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  gp.error = error;
+  gp.timeout_ns = 2000000000ull;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = rows_padded == 16 ? launch_gemm<16>(gp, tiles, splits, st)
+                  : rows_padded == 32 ? launch_gemm<32>(gp, tiles, splits, st)
+                                      : launch_gemm<64>(gp, tiles, splits, st);
+  if (e != cudaSuccess) return fail(MK_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
+  if (splits > 1) {
+    const int bn = rows * n;
+    mk::gemm_reduce_kernel<<<(bn + 255) / 256, 256, 0, st>>>(
+        static_cast<const float*>(workspace), splits, bn, static_cast<const mk::bf16*>(residual),
+        static_cast<mk::bf16*>(out), out_f32);
+    MK_CUDA(cudaGetLastError());
+  }
   return MK_OK;
 }
 

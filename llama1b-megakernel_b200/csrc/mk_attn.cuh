@@ -50,6 +50,18 @@ __device__ __forceinline__ float2 bf2x2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
+// c0 += lo(a) lo(b), c1 += hi(a) hi(b) on packed bf16 pairs, in fp32 (the
+// products of two bf16 values are exact in fp32).
+__device__ __forceinline__ void attn_fma2(uint32_t a, uint32_t b, float& c0, float& c1) {
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\t"
+      "mov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+      "fma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "r"(a), "r"(b));
+}
+
 __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __grid_constant__ PagedAttnParams p) {
   __shared__ float pw[kAttnCtaWarps][4][32];               // probabilities of a chunk
   __shared__ uint4 vbuf[kAttnCtaWarps][32][8];             // a chunk's V rows
@@ -60,19 +72,17 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
   const int h = lane & 3, r8 = lane >> 2;
   const int len = p.lengths[b];
   const int p0 = s * kAttnSplitLen, p1 = min(len, p0 + kAttnSplitLen);
-  float q[64];
+  // q head h as packed bf16 (the scale is applied to the fp32 score)
+  uint32_t q[32];
   {
     const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.NQ + g * 4 + h) * 64);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const uint4 u = __ldg(qp + c);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = bf2x2(w[e]);
-        q[c * 8 + 2 * e] = f.x * p.scale;
-        q[c * 8 + 2 * e + 1] = f.y * p.scale;
-      }
+      q[c * 4 + 0] = u.x;
+      q[c * 4 + 1] = u.y;
+      q[c * 4 + 2] = u.z;
+      q[c * 4 + 3] = u.w;
     }
   }
   float m = -INFINITY, l = 0.f;  // head h's running max and sum (same in its 8 lanes)
@@ -122,19 +132,16 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
     float cm = -INFINITY;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      float a0 = 0.f, a1 = 0.f;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 u = kok[r] ? kp[r][c] : make_uint4(0u, 0u, 0u, 0u);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = bf2x2(w[e]);
-          a0 = fmaf(f.x, q[c * 8 + 2 * e], a0);
-          a1 = fmaf(f.y, q[c * 8 + 2 * e + 1], a1);
-        }
+        attn_fma2(u.x, q[c * 4 + 0], a0, a1);
+        attn_fma2(u.y, q[c * 4 + 1], a2, a3);
+        attn_fma2(u.z, q[c * 4 + 2], a0, a1);
+        attn_fma2(u.w, q[c * 4 + 3], a2, a3);
       }
-      sc[r] = kok[r] ? a0 + a1 : -INFINITY;
+      sc[r] = kok[r] ? ((a0 + a1) + (a2 + a3)) * p.scale : -INFINITY;
       cm = fmaxf(cm, sc[r]);
     }
     // head h's max and sum over the chunk: its 8 lanes differ in lane bits 2..4

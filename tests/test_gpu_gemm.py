@@ -1,0 +1,67 @@
+"""The tcgen05 skinny GEMM (``mk_gemm_bf16``, csrc/mk_gemm.cuh) against fp64 sums.
+
+Y = X W^T (+ R) for the batched decode shapes: every output within one bf16
+rounding (2^-7 relative, 1e-4 absolute for the fp32 sum) of the exactly summed
+product of the same bf16 inputs, fp32 outputs within 1e-4, for padded batches 16 / 32 / 64 with fewer real rows, with
+and without the split along K, with a residual, and with fp32 output.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+from llama1b_megakernel_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(lib, w, x, rows, residual=None, f32=False):
+    n, k = w.shape
+    bp = x.shape[0]
+    dev = w.device
+    out = torch.empty(rows, n, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
+    ws = lib.mk_gemm_workspace(n, k, rows)
+    work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(lib.mk_gemm_bf16(
+        w.data_ptr(), n, k, x.data_ptr(), rows, bp,
+        residual.data_ptr() if residual is not None else None,
+        None if f32 else out.data_ptr(), out.data_ptr() if f32 else None,
+        work.data_ptr(), work.numel(), err.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert int(err[0]) == 0
+    return out
+
+
+@pytest.mark.parametrize("n,k,rows,bp", [(3072, 2048, 8, 16), (2048, 2048, 32, 32),
+                                         (16384, 2048, 64, 64), (2048, 8192, 20, 32),
+                                         (128 * 11, 192, 1, 16)])
+def test_gemm_matches_exact_sum(n, k, rows, bp):
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(n + k + rows)
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    x = torch.zeros(bp, k, dtype=torch.bfloat16, device="cuda")
+    x[:rows] = torch.randn(rows, k, generator=g, device="cuda").bfloat16()
+    res = torch.randn(rows, n, generator=g, device="cuda").bfloat16()
+    exact = x[:rows].double() @ w.double().T
+    y = _run(lib, w, x, rows)
+    # one bf16 rounding (<= 2^-8 relative) of an fp32 sum (absolute slack 1e-4)
+    assert ((y.double() - exact).abs() <= exact.abs() * 2.0 ** -7 + 1e-4).all()
+    yr = _run(lib, w, x, rows, residual=res)
+    er = exact + res.double()
+    assert ((yr.double() - er).abs() <= er.abs() * 2.0 ** -7 + 1e-4).all()
+    yf = _run(lib, w, x, rows, f32=True)
+    assert ((yf.double() - exact).abs() <= exact.abs() * 1e-4 + 1e-4).all()
+
+
+def test_gemm_rejects_bad_shapes():
+    lib = _lib.load()
+    w = torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros(16, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(1, 100, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = lib.mk_gemm_bf16(w.data_ptr(), 100, 64, x.data_ptr(), 1, 16, None, out.data_ptr(), None,
+                          None, 0, err.data_ptr(), None)
+    assert rc == _lib.MK_EINVAL
