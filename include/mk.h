@@ -249,7 +249,7 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
 /* Skinny GEMM on the tcgen05 tensor cores for the batched decode path:
  * Y[rows][n] = X[rows][k] . W[n][k]^T (+ residual[rows][n]), bf16 inputs,
  * fp32 accumulation, Y bf16 (out) or fp32 (out_f32, no residual). W is a
- * weight matrix in HF [out][in] layout (n a multiple of 128, k of 64); X has
+ * weight matrix in HF [out][in] layout (any n, k a multiple of 64); X has
  * rows_padded (16, 32 or 64) rows of which the first `rows` are real and the
  * rest zero. Narrow W is split along k across CTAs; then `workspace` must
  * hold mk_gemm_workspace(n, k, rows) bytes. *error (device) records a wait

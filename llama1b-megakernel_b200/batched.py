@@ -11,12 +11,13 @@ path runs one step as:
   (``mk_rope_scatter``, which reads the RoPE-pair column order directly),
   attention by this library's paged split-K decode kernel
   (``mk_paged_attention``, csrc/mk_attn.cuh: the HBM-heavy part), o_proj with
-  the residual added by the GEMM (``addmm``), RMSNorm, the gate/up GEMM,
+  the residual added by the GEMM, RMSNorm, the gate/up GEMM,
   ``mk_swiglu``, down with the residual; then the final norm, lm_head and
   argmax;
-* the GEMMs are cuBLAS (tensor cores) through torch on the kernel's own packed
-  weights; the elementwise steps are this library's fused kernels
-  (csrc/mk_batched.cuh);
+* the GEMMs are this library's tcgen05 skinny GEMM (``mk_gemm_bf16``,
+  csrc/mk_gemm.cuh) on the kernel's own packed weights, the residual added in
+  its epilogue and the logits written in fp32; the elementwise steps are the
+  fused kernels of csrc/mk_batched.cuh;
 * the whole step is captured once per batch size into a CUDA graph, so a step
   is one graph launch with the tokens and positions on the device.
 
@@ -30,7 +31,6 @@ from __future__ import annotations
 import ctypes
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from .kv_cache import PagedKVCache
@@ -44,6 +44,8 @@ class BatchedDecoder:
                  num_pages: int | None = None):
         if getattr(model, "tp_world", 1) != 1:
             raise NotImplementedError("the batched path runs on one GPU")
+        if not 1 <= max_batch <= 64:
+            raise ValueError(f"max_batch {max_batch} outside [1, 64] (the GEMM's padded batch)")
         if max_seq_len > model.rope_len:
             raise ValueError(f"max_seq_len {max_seq_len} exceeds the model's RoPE table "
                              f"({model.rope_len} positions)")
@@ -57,6 +59,11 @@ class BatchedDecoder:
         self.lib = model.lib
         ws = self.lib.mk_paged_attention_workspace(max_batch, self.cfg.num_kv_heads, max_seq_len)
         self.work = torch.empty(max(ws, 16), dtype=torch.uint8, device=self.dev)
+        c = self.cfg
+        gws = max(self.lib.mk_gemm_workspace(n, k, max_batch) for n, k in (
+            ((c.num_q_heads + 2 * c.num_kv_heads) * 64, c.hidden), (c.hidden, c.num_q_heads * 64),
+            (2 * c.intermediate, c.hidden), (c.hidden, c.intermediate), (c.vocab, c.hidden)))
+        self.gwork = torch.empty(max(gws, 16), dtype=torch.uint8, device=self.dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self._graphs: dict[int, tuple] = {}
 
@@ -70,39 +77,56 @@ class BatchedDecoder:
             ctypes.c_float(c.head_dim ** -0.5), self.work.data_ptr(), self.work.numel(),
             out.data_ptr(), self.err.data_ptr(), torch.cuda.current_stream().cuda_stream))
 
-    def _step(self, tokens, positions, logits_out, ids_out):
+    def _gemm(self, w, x, rows, out=None, out_f32=None, residual=None):
+        """Y = X W^T (+ residual) on the tensor cores (``mk_gemm_bf16``); X has
+        the padded row count, its first ``rows`` rows real."""
+        n, k = w.shape
+        _lib.check(self.lib.mk_gemm_bf16(
+            w.data_ptr(), n, k, x.data_ptr(), rows, x.shape[0],
+            residual.data_ptr() if residual is not None else None,
+            out.data_ptr() if out is not None else None,
+            out_f32.data_ptr() if out_f32 is not None else None,
+            self.gwork.data_ptr(), self.gwork.numel(), self.err.data_ptr(),
+            torch.cuda.current_stream().cuda_stream))
+
+    def _buffers(self, B: int) -> dict:
+        c, dev = self.cfg, self.dev
+        BP = 16 if B <= 16 else 32 if B <= 32 else 64
+        nh = c.num_q_heads + 2 * c.num_kv_heads
+        z = lambda *shape: torch.zeros(*shape, dtype=torch.bfloat16, device=dev)  # noqa: E731
+        return dict(x=z(B, c.hidden), h=z(BP, c.hidden), q=z(B, c.num_q_heads, 64),
+                    attn=z(BP, c.num_q_heads * 64), act=z(BP, c.intermediate),
+                    qkv=z(B, nh * 64), gu=z(B, 2 * c.intermediate))
+
+    def _step(self, tokens, positions, logits_out, ids_out, buf):
         c, pw, kv, lib = self.cfg, self.m.packed, self.kv, self.lib
         B = tokens.numel()
         H, NQ, NKV, I = c.hidden, c.num_q_heads, c.num_kv_heads, c.intermediate
         st = torch.cuda.current_stream().cuda_stream
-        dev = self.dev
-        x = pw.embed[tokens.long()]
+        x, h, q, attn, act, qkv, gu = (buf[k] for k in ("x", "h", "q", "attn", "act", "qkv", "gu"))
+        x.copy_(pw.embed[tokens.long()])
         lengths = (positions + 1).to(torch.int32)
-        h = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
-        q = torch.empty(B, NQ, 64, dtype=torch.bfloat16, device=dev)
-        attn = torch.empty(B, NQ, 64, dtype=torch.bfloat16, device=dev)
-        act = torch.empty(B, I, dtype=torch.bfloat16, device=dev)
+        eps = ctypes.c_float(c.rms_eps)
         for l in range(c.num_layers):
-            _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_attn[l].data_ptr(),
-                                           ctypes.c_float(c.rms_eps), B, H, h.data_ptr(), st))
-            qkv = F.linear(h, pw.w_qkv[l].view(-1, H))  # packed RoPE-pair column order
+            _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_attn[l].data_ptr(), eps, B, H,
+                                           h.data_ptr(), st))
+            self._gemm(pw.w_qkv[l].view(-1, H), h, B, out=qkv)  # packed RoPE-pair column order
             _lib.check(lib.mk_rope_scatter(
                 qkv.data_ptr(), pw.rope_cos.data_ptr(), pw.rope_sin.data_ptr(),
                 positions.data_ptr(), kv.block_tables.data_ptr(), kv.max_blocks, kv.num_pages,
                 kv.page_size, NQ, NKV, B, q.data_ptr(), kv.k_pages[l].data_ptr(),
                 kv.v_pages[l].data_ptr(), self.err.data_ptr(), st))
             self._attention(q, l, lengths, B, attn)
-            x = torch.addmm(x, attn.view(B, NQ * 64), pw.w_o[l].t())  # residual in the GEMM
-            _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_mlp[l].data_ptr(),
-                                           ctypes.c_float(c.rms_eps), B, H, h.data_ptr(), st))
-            gu = F.linear(h, pw.w_gate_up[l].view(2 * I, H))  # (gate, up) interleaved
+            self._gemm(pw.w_o[l], attn, B, out=x, residual=x)  # x += o_proj(attn)
+            _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_mlp[l].data_ptr(), eps, B, H,
+                                           h.data_ptr(), st))
+            self._gemm(pw.w_gate_up[l].view(2 * I, H), h, B, out=gu)  # (gate, up) interleaved
             _lib.check(lib.mk_swiglu(gu.data_ptr(), B * I, act.data_ptr(), st))
-            x = torch.addmm(x, act, pw.w_down[l].t())
-        _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_final.data_ptr(),
-                                       ctypes.c_float(c.rms_eps), B, H, h.data_ptr(), st))
-        lg = F.linear(h, pw.embed)
-        logits_out.copy_(lg)
-        ids_out.copy_(lg.argmax(dim=-1))
+            self._gemm(pw.w_down[l], act, B, out=x, residual=x)
+        _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_final.data_ptr(), eps, B, H,
+                                       h.data_ptr(), st))
+        self._gemm(pw.embed, h, B, out_f32=logits_out)
+        ids_out.copy_(logits_out.argmax(dim=-1))
 
     def _graph(self, B: int):
         g = self._graphs.get(B)
@@ -112,6 +136,7 @@ class BatchedDecoder:
             pos = torch.zeros(B, dtype=torch.int32, device=dev)
             logits = torch.empty(B, self.cfg.vocab, dtype=torch.float32, device=dev)
             ids = torch.empty(B, dtype=torch.int64, device=dev)
+            buf = self._buffers(B)
             # warm up on a side stream, then capture. The warm-up really runs
             # (token 0 at position 0 of every slot), so the cache rows it
             # overwrites are saved and put back; capturing runs nothing.
@@ -123,14 +148,14 @@ class BatchedDecoder:
             s = torch.cuda.Stream(device=dev)
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
-                self._step(tok, pos, logits, ids)
+                self._step(tok, pos, logits, ids, buf)
             torch.cuda.current_stream().wait_stream(s)
             kv.k_pages[:, page0, :, 0] = saved[0]
             kv.v_pages[:, page0, :, 0] = saved[1]
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                self._step(tok, pos, logits, ids)
-            g = (graph, tok, pos, logits, ids)
+                self._step(tok, pos, logits, ids, buf)
+            g = (graph, tok, pos, logits, ids, buf)
             self._graphs[B] = g
         return g
 
@@ -147,7 +172,7 @@ class BatchedDecoder:
             raise ValueError(f"positions must be in [0, {self.max_seq_len})")
         for b in range(B):
             self.kv.reserve(b, int(pos_host[b]) + 1)
-        graph, tok, pos, logits, ids = self._graph(B)
+        graph, tok, pos, logits, ids, _ = self._graph(B)
         tok.copy_(torch.as_tensor(tokens).to(tok.device, torch.int32).reshape(-1))
         pos.copy_(pos_host.to(pos.device, torch.int32).reshape(-1))
         graph.replay()

@@ -398,7 +398,7 @@ int encode_sw128(CUtensorMap* out, const void* base, long long rows, long long c
 // K blocks per split for an n x k GEMM: narrow W is split along K so the
 // grid covers the SMs.
 int gemm_kblocks_per_split(int n, int k, int sms) {
-  const int tiles = n / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
+  const int tiles = (n + mk::kGemmTileN - 1) / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
   int splits = tiles >= sms / 2 ? 1 : (sms + tiles - 1) / tiles;
   if (splits > kblocks) splits = kblocks;
   return (kblocks + splits - 1) / splits;
@@ -793,7 +793,7 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
 int64_t mk_gemm_workspace(int32_t n, int32_t k, int32_t rows) {
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (n < mk::kGemmTileN || k < mk::kGemmTileK || rows < 1) return 0;
+  if (n < 1 || k < mk::kGemmTileK || rows < 1) return 0;
   const int kps = gemm_kblocks_per_split(n, k, sms);
   const int splits = (k / mk::kGemmTileK + kps - 1) / kps;
   return splits > 1 ? (int64_t)splits * rows * n * 4 : 0;
@@ -804,8 +804,8 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
                  void* workspace, int64_t workspace_bytes, int32_t* error, void* stream) {
   if (!w || !x || !error || (!out && !out_f32) || (out && out_f32))
     return fail(MK_EINVAL, "w, x, error and exactly one of out / out_f32 are required");
-  if (n < mk::kGemmTileN || n % mk::kGemmTileN || k < mk::kGemmTileK || k % mk::kGemmTileK)
-    return fail(MK_EINVAL, "n must be a multiple of 128 and k of 64 (n %d, k %d)", n, k);
+  if (n < 1 || k < mk::kGemmTileK || k % mk::kGemmTileK)
+    return fail(MK_EINVAL, "k must be a positive multiple of 64 and n positive (n %d, k %d)", n, k);
   if (rows_padded != 16 && rows_padded != 32 && rows_padded != 64)
     return fail(MK_EINVAL, "rows_padded must be 16, 32 or 64 (got %d)", rows_padded);
   if (rows < 1 || rows > rows_padded) return fail(MK_EINVAL, "rows %d outside [1, %d]", rows, rows_padded);
@@ -814,7 +814,7 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
   int dev = 0, sms = 148;
   MK_CUDA(cudaGetDevice(&dev));
   MK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int tiles = n / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
+  const int tiles = (n + mk::kGemmTileN - 1) / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
   const int kps = gemm_kblocks_per_split(n, k, sms);
   const int splits = (kblocks + kps - 1) / kps;
   if (splits > 1 && (!workspace || workspace_bytes < (int64_t)splits * rows * n * 4))

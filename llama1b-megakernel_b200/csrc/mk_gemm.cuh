@@ -4,8 +4,9 @@
 // At bs 8-64 the decode projections are "skinny" GEMMs: W (the weights, N x
 // K, K contiguous) is large and read once, X (the activations) has 8-64 rows.
 // One CTA computes a 128-row tile of W against all of X:
-//  * A = the W tile (128 rows), B = X (BP rows: the batch padded to 16, 32 or
-//    64 with zero rows), both K-major with the 128-byte swizzle, loaded by 2-D
+//  * A = the W tile (128 rows; past N the TMA fills zeros), B = X (BP rows:
+//    the batch padded to 16, 32 or 64 with zero rows), both K-major with the
+//    128-byte swizzle, loaded by 2-D
 //    TMA boxes of 64 columns (no multicast) into a ring of kGemmStages stages
 //    with full/empty mbarriers;
 //  * one lane issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32, M = 128,
@@ -27,7 +28,7 @@
 
 namespace mk {
 
-constexpr int kGemmStages = 8;
+constexpr int kGemmStages = 4;  // 96 KB: two CTAs per SM overlap one tile's epilogue with the next's loads
 constexpr int kGemmTileN = 128;  // W rows per CTA (the MMA's M)
 constexpr int kGemmTileK = 64;   // columns per stage: one 128-byte swizzle atom per row
 constexpr int kGemmThreads = 128;
@@ -136,7 +137,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[BP]) {
 }
 
 template <int BP>
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t gsm[];
   constexpr uint32_t kA = kGemmTileN * kGemmTileK * 2;  // 16 KB
   constexpr uint32_t kB = BP * kGemmTileK * 2;
@@ -234,8 +235,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   float v[BP];
   tmem_ld_cols<BP>(tmem + ((uint32_t)(warp * 32) << 16), v);
-  if (good) {
-    const int n = tile * kGemmTileN + warp * 32 + lane;
+  const int n = tile * kGemmTileN + warp * 32 + lane;
+  if (good && n < p.N) {  // rows past N (the last tile's) were zero-filled by TMA
 #pragma unroll
     for (int b = 0; b < BP; ++b) {
       if (b >= p.B) break;

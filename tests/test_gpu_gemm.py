@@ -37,7 +37,7 @@ def _run(lib, w, x, rows, residual=None, f32=False):
 
 @pytest.mark.parametrize("n,k,rows,bp", [(3072, 2048, 8, 16), (2048, 2048, 32, 32),
                                          (16384, 2048, 64, 64), (2048, 8192, 20, 32),
-                                         (128 * 11, 192, 1, 16)])
+                                         (128 * 11, 192, 1, 16), (5003, 512, 3, 16)])
 def test_gemm_matches_exact_sum(n, k, rows, bp):
     lib = _lib.load()
     g = torch.Generator(device="cuda").manual_seed(n + k + rows)
@@ -58,10 +58,10 @@ def test_gemm_matches_exact_sum(n, k, rows, bp):
 
 def test_gemm_rejects_bad_shapes():
     lib = _lib.load()
-    w = torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda")
-    x = torch.zeros(16, 64, dtype=torch.bfloat16, device="cuda")
-    out = torch.empty(1, 100, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(128, 100, dtype=torch.bfloat16, device="cuda")  # k not a multiple of 64
+    x = torch.zeros(16, 100, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(1, 128, dtype=torch.bfloat16, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    rc = lib.mk_gemm_bf16(w.data_ptr(), 100, 64, x.data_ptr(), 1, 16, None, out.data_ptr(), None,
+    rc = lib.mk_gemm_bf16(w.data_ptr(), 128, 100, x.data_ptr(), 1, 16, None, out.data_ptr(), None,
                           None, 0, err.data_ptr(), None)
     assert rc == _lib.MK_EINVAL
