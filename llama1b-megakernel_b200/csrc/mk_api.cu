@@ -418,6 +418,28 @@ cudaError_t launch_gemm(const mk::GemmParams& gp, int tiles, int splits, cudaStr
 }
 }  // namespace
 
+namespace {
+// Positions per attention CTA: long enough for every warp to pipeline a few
+// chunks, short enough that batch x kv heads x splits fills the GPU (3 CTAs
+// per SM), a multiple of 128.
+int attn_split_len(int batch, int num_kv_heads, int max_len, int sms) {
+  const long long items = (long long)batch * num_kv_heads;
+  const long long target = 3LL * sms;
+  long long splits = (target + items - 1) / items;
+  if (splits < 1) splits = 1;
+  long long len = (max_len + splits - 1) / splits;
+  len = ((len + 127) / 128) * 128;
+  if (len < 128) len = 128;
+  if (len > 1024) len = 1024;
+  return (int)len;
+}
+int device_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+}  // namespace
+
 extern "C" {
 
 int mk_init(const MkConfig* cfg, int device, MkModel** out) {
@@ -742,9 +764,11 @@ int mk_schedule_gap(const MkConfig* cfg, int32_t batch, int32_t grid, int32_t* g
 
 const char* mk_last_error(void) { return g_last_error.c_str(); }
 
+
 int64_t mk_paged_attention_workspace(int32_t batch, int32_t num_kv_heads, int32_t max_len) {
   if (batch < 1 || num_kv_heads < 1 || max_len < 1) return 0;
-  const int64_t splits = (max_len + mk::kAttnSplitLen - 1) / mk::kAttnSplitLen;
+  const int sl = attn_split_len(batch, num_kv_heads, max_len, device_sms());
+  const int64_t splits = (max_len + sl - 1) / sl;
   return (int64_t)batch * num_kv_heads * splits * 4 * mk::kAttnPartial * 4;
 }
 
@@ -777,13 +801,20 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
   ap.ps = page_size;
   ap.max_blocks = max_blocks;
   ap.num_pages = num_pages;
-  ap.splits = (max_len + mk::kAttnSplitLen - 1) / mk::kAttnSplitLen;
+  ap.split_len = attn_split_len(batch, num_kv_heads, max_len, device_sms());
+  ap.splits = (max_len + ap.split_len - 1) / ap.split_len;
   ap.scale = scale;
   ap.work = static_cast<float*>(workspace);
   ap.out = static_cast<mk::bf16*>(out);
   ap.error = error;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  mk::paged_attn_kernel<<<dim3(ap.splits, num_kv_heads, batch), mk::kAttnCtaWarps * 32, 0, st>>>(ap);
+  static bool attr = false;
+  if (!attr) {
+    MK_CUDA(cudaFuncSetAttribute(mk::paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 mk::kAttnSmem));
+    attr = true;
+  }
+  mk::paged_attn_kernel<<<dim3(ap.splits, num_kv_heads, batch), mk::kAttnCtaWarps * 32, mk::kAttnSmem, st>>>(ap);
   MK_CUDA(cudaGetLastError());
   mk::paged_attn_merge_kernel<<<dim3(num_kv_heads, batch), 256, 0, st>>>(ap);
   MK_CUDA(cudaGetLastError());

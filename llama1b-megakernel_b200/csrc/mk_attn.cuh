@@ -7,14 +7,16 @@
 // as much as the weights at bs 64, so this kernel is built to stream it:
 //
 //  * grid (splits, kv heads, sequences); CTA (s, g, b) covers positions
-//    [s * kAttnSplitLen, (s+1) * kAttnSplitLen) of sequence b for the 4 q
-//    heads of kv head g, 4 warps over 32-position chunks of it;
-//  * a 32-position chunk is read in the natural orientation of each product:
-//    for the scores lane (r, h) dots q head h (in registers) with the K rows
-//    of positions r, r+8, r+16, r+24 (four lanes share each row load); the V
-//    rows go through shared memory (8 independent 16-byte loads per lane,
-//    issued before the scores) and for P . V lane j owns dims 2j, 2j+1 of all
-//    32 rows, for the 4 heads;
+//    [s * split_len, (s+1) * split_len) of sequence b for the 4 q heads of kv
+//    head g; its 4 warps take turns at the 32-position chunks of the split;
+//  * each warp pipelines its chunks: cp.async copies the next chunk's K and V
+//    rows (16-byte pieces, zero-filled past the end) into the other of two
+//    shared buffers while it computes the current one, whose pieces are
+//    XOR-swizzled by row so both products read shared memory without bank
+//    conflicts;
+//  * scores: lane (r, h) dots q head h (packed bf16 in registers,
+//    fma.rn.f32.bf16) with rows r, r+8, r+16, r+24; P . V: lane j owns dims
+//    2j, 2j+1 of all 32 rows for the 4 heads;
 //  * online softmax in fp32 per head; the CTA's warps are merged in shared
 //    memory, and the CTA writes one (m, l, o[64]) partial per head;
 //  * a merge kernel (one CTA per sequence and kv head) combines the splits and
@@ -29,9 +31,11 @@
 
 namespace mk {
 
-constexpr int kAttnSplitLen = 128;  // positions per CTA
 constexpr int kAttnCtaWarps = 4;
 constexpr int kAttnPartial = 2 + 64;  // m, l, o[64]
+constexpr int kAttnChunkBytes = 32 * 128;  // 32 rows of K (or V)
+// Shared memory per CTA: per warp two chunk buffers of K and V.
+constexpr int kAttnSmem = kAttnCtaWarps * 2 * 2 * kAttnChunkBytes;
 
 struct PagedAttnParams {
   const __nv_bfloat16* q;      // [B][NQ][64]
@@ -39,7 +43,7 @@ struct PagedAttnParams {
   const __nv_bfloat16* v;
   const int* block_tables;     // [B][max_blocks]
   const int* lengths;          // [B]: positions [0, len) are attended
-  int NQ, NKV, ps, max_blocks, num_pages, splits;
+  int NQ, NKV, ps, max_blocks, num_pages, splits, split_len;
   float scale;
   float* work;                 // [B][NKV][splits][4][kAttnPartial]
   __nv_bfloat16* out;          // [B][NQ][64]
@@ -62,16 +66,58 @@ __device__ __forceinline__ void attn_fma2(uint32_t a, uint32_t b, float& c0, flo
       : "r"(a), "r"(b));
 }
 
+// 16-byte asynchronous copy global -> shared; src_bytes 0 fills zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// Row r's 16-byte piece c of a chunk buffer sits at piece c ^ (r & 7): the 8
+// rows a score instruction reads, and the 8 pieces a P . V instruction reads,
+// fall in different banks.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
 __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __grid_constant__ PagedAttnParams p) {
+  extern __shared__ __align__(128) uint8_t asmem[];
   __shared__ float pw[kAttnCtaWarps][4][32];               // probabilities of a chunk
-  __shared__ uint4 vbuf[kAttnCtaWarps][32][8];             // a chunk's V rows
   __shared__ float st[kAttnCtaWarps][4][kAttnPartial];     // per-warp states
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // scores: lane = (position r8 of each 8, head h); P . V: lane = dims 2 lane, 2 lane + 1
   const int h = lane & 3, r8 = lane >> 2;
   const int len = p.lengths[b];
-  const int p0 = s * kAttnSplitLen, p1 = min(len, p0 + kAttnSplitLen);
+  const int p0 = s * p.split_len, p1 = min(len, p0 + p.split_len);
+  const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(asmem) + warp * 4 * kAttnChunkBytes;
+  // buffer j (0, 1): K at wbuf + j * 2 * kAttnChunkBytes, V right after it
+  const int* table = p.block_tables + (size_t)b * p.max_blocks;
+  const int nchunks = p1 > p0 ? (p1 - p0 + 31) / 32 : 0;
+  // this warp takes chunks warp, warp + 4, ... of the split
+  auto issue = [&](int ci, int j) {
+    const int c0 = p0 + ci * 32;
+    const uint32_t kb = wbuf + j * 2 * kAttnChunkBytes, vb = kb + kAttnChunkBytes;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = k * 4 + (lane >> 3), piece = lane & 7, pos = c0 + row;
+      const __nv_bfloat16* ks = p.k;
+      const __nv_bfloat16* vs = p.v;
+      uint32_t bytes = 0;
+      if (pos < p1) {
+        const int page = table[pos / p.ps];
+        if (page >= 0 && page < p.num_pages) {
+          const size_t off = (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64 + piece * 8;
+          ks += off;
+          vs += off;
+          bytes = 16;
+        } else {
+          atomicExch(p.error, 1);
+        }
+      }
+      cp_async16(kb + swz(row, piece), ks, bytes);
+      cp_async16(vb + swz(row, piece), vs, bytes);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
   // q head h as packed bf16 (the scale is applied to the fp32 score)
   uint32_t q[32];
   {
@@ -89,59 +135,39 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
   float o[4][2];
 #pragma unroll
   for (int hh = 0; hh < 4; ++hh) o[hh][0] = o[hh][1] = 0.f;
-  const int* table = p.block_tables + (size_t)b * p.max_blocks;
-  for (int c0 = p0 + warp * 32; c0 < p1; c0 += kAttnCtaWarps * 32) {
-    // V rows of the chunk into shared memory: 8 independent 16-byte loads per
-    // lane, 4 rows per load instruction (rows past the end or in a bad page: 0)
-    {
-      uint4 t[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int row = k * 4 + (lane >> 3), pos = c0 + row;
-        t[k] = make_uint4(0u, 0u, 0u, 0u);
-        if (pos < p1) {
-          const int page = table[pos / p.ps];
-          if (page >= 0 && page < p.num_pages)
-            t[k] = reinterpret_cast<const uint4*>(
-                p.v + (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64)[lane & 7];
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) vbuf[warp][k * 4 + (lane >> 3)][lane & 7] = t[k];
+
+  int j = 0;
+  if (warp < nchunks) issue(warp, 0);
+  for (int ci = warp; ci < nchunks; ci += kAttnCtaWarps, j ^= 1) {
+    if (ci + kAttnCtaWarps < nchunks) {
+      issue(ci + kAttnCtaWarps, j ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    // scores: addresses of the 4 positions first, then all 32 loads
-    const uint4* kp[4];
-    bool kok[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int pos = c0 + r * 8 + r8;
-      kok[r] = false;
-      kp[r] = reinterpret_cast<const uint4*>(p.k);
-      if (pos < p1) {
-        const int page = table[pos / p.ps];
-        if (page < 0 || page >= p.num_pages) {
-          atomicExch(p.error, 1);
-        } else {
-          kok[r] = true;
-          kp[r] = reinterpret_cast<const uint4*>(
-              p.k + (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64);
-        }
-      }
-    }
+    __syncwarp();
+    const int c0 = p0 + ci * 32;
+    const uint32_t kb = wbuf + j * 2 * kAttnChunkBytes, vb = kb + kAttnChunkBytes;
+    // ---- scores from shared memory
     float sc[4];
     float cm = -INFINITY;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
+      const int row = r * 8 + r8;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint4 u = kok[r] ? kp[r][c] : make_uint4(0u, 0u, 0u, 0u);
+        uint4 u;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                     : "r"(kb + swz(row, c)));
         attn_fma2(u.x, q[c * 4 + 0], a0, a1);
         attn_fma2(u.y, q[c * 4 + 1], a2, a3);
         attn_fma2(u.z, q[c * 4 + 2], a0, a1);
         attn_fma2(u.w, q[c * 4 + 3], a2, a3);
       }
-      sc[r] = kok[r] ? ((a0 + a1) + (a2 + a3)) * p.scale : -INFINITY;
+      const int pos = c0 + row;
+      sc[r] = pos < p1 ? ((a0 + a1) + (a2 + a3)) * p.scale : -INFINITY;
       cm = fmaxf(cm, sc[r]);
     }
     // head h's max and sum over the chunk: its 8 lanes differ in lane bits 2..4
@@ -161,7 +187,7 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
     l = l * alpha + sum;
     m = mn;
     __syncwarp();
-    // ---- P . V
+    // ---- P . V from shared memory
 #pragma unroll
     for (int hh = 0; hh < 4; ++hh) {
       const float a = __shfl_sync(0xffffffffu, alpha, hh);  // lane hh holds head hh
@@ -169,12 +195,15 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
       o[hh][1] *= a;
     }
     const int n = min(32, p1 - c0);
-    for (int j = 0; j < n; ++j) {
-      const uint32_t vw = reinterpret_cast<const uint32_t*>(&vbuf[warp][j][0])[lane];
+    for (int jj = 0; jj < n; ++jj) {
+      uint32_t vw;
+      asm volatile("ld.shared.u32 %0, [%1];"
+                   : "=r"(vw)
+                   : "r"(vb + swz(jj, lane >> 2) + (lane & 3) * 4));
       const float2 f = bf2x2(vw);
 #pragma unroll
       for (int hh = 0; hh < 4; ++hh) {
-        const float pr = pw[warp][hh][j];
+        const float pr = pw[warp][hh][jj];
         o[hh][0] = fmaf(pr, f.x, o[hh][0]);
         o[hh][1] = fmaf(pr, f.y, o[hh][1]);
       }

@@ -233,13 +233,14 @@ struct Polled {
   int ok;
 };
 
-// Slow path of poll_tagged: re-read until the tags match (time-bounded).
+// Slow path of poll_tagged: re-read until the tags match (time-bounded). No
+// sleep between reads: the wait is on the step's critical path (a 64 ns
+// sleep cost 2.5% of the step, measured).
 // Returns by value so callers' registers stay out of local memory.
 __device__ __noinline__ Polled poll_tagged_slow(const Params& p, const uint32_t* src, uint32_t tag,
                                                 int where) {
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
-    __nanosleep(64);
     const uint4 u = __ldcg(reinterpret_cast<const uint4*>(src));
     if (tags_ok(u, tag)) return {u, 1};
     if ((it & 15) == 0) {
@@ -302,7 +303,6 @@ __device__ __noinline__ Summed tp_sum(const Params& p, int slot, int b, int u, u
     unsigned long long v = ld_sys_u64(w);
     for (uint32_t it = 1; (uint32_t)(v >> 32) != tag; ++it) {
       if (!t0) t0 = global_ns();
-      __nanosleep(64);
       v = ld_sys_u64(w);
       if ((it & 15) == 0) {
         if (aborted(p)) return {0.f, 0};
