@@ -65,9 +65,13 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a few steps, no e2e / sweep / cpu baseline")
-    ap.add_argument("--case", choices=["small4"], default=None,
-                    help="small4: ncu profiling case - 4 Llama-3.2-1B layers, vocab 32000, one "
-                         "step at ctx 512 after 4 warm-up steps (prints its time, no JSON line)")
+    ap.add_argument("--case", choices=["small4", "gemm", "batched"], default=None,
+                    help="ncu profiling cases (print timings, no JSON line): small4 - 4 "
+                         "Llama-3.2-1B layers, vocab 32000, one step at ctx 512 after 4 warm-up "
+                         "steps; gemm - the tcgen05 GEMM on the batched projection shapes at 8 "
+                         "and 64 rows (3 warm-up + 7 timed launches each, L2 flushed, cuBLAS "
+                         "beside it); batched - one bs-64 batched step at KV 1024 replayed "
+                         "inside the NVTX range 'replay'")
     return ap.parse_args()
 
 
@@ -475,6 +479,74 @@ def run_batched(model, cfg, dev, hbm_peak):
     return res
 
 
+def run_case_gemm():
+    """The tcgen05 GEMM (mk_gemm_bf16) alone on the batched decode shapes."""
+    import ctypes  # noqa: F401
+
+    from llama1b_megakernel_b200 import _lib
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    for rows, bp in ((8, 16), (64, 64)):
+        for n, k in ((3072, 2048), (2048, 2048), (16384, 2048), (2048, 8192), (128256, 2048)):
+            w = (torch.randn(n, k, device=dev) * 0.02).bfloat16()
+            x = torch.zeros(bp, k, dtype=torch.bfloat16, device=dev)
+            x[:rows] = torch.randn(rows, k, device=dev).bfloat16()
+            out = torch.empty(rows, n, dtype=torch.bfloat16, device=dev)
+            ws = lib.mk_gemm_workspace(n, k, rows)
+            work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+
+            def run():
+                _lib.check(lib.mk_gemm_bf16(w.data_ptr(), n, k, x.data_ptr(), rows, bp, None,
+                                            out.data_ptr(), None, work.data_ptr(), work.numel(),
+                                            err.data_ptr(), torch.cuda.current_stream().cuda_stream))
+
+            for _ in range(3):
+                run()
+            ts, tc = [], []
+            for _ in range(7):
+                for fn, acc in ((run, ts), (lambda: torch.nn.functional.linear(x[:rows], w), tc)):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    fn()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    acc.append(e0.elapsed_time(e1))
+            t, tcb = statistics.median(ts), statistics.median(tc)
+            print(f"rows {rows:3d} n {n:6d} k {k:5d}: mk_gemm_bf16 {t * 1e3:7.1f} us "
+                  f"({n * k * 2 / t / 1e6:5.0f} GB/s), cuBLAS {tcb * 1e3:7.1f} us  err {int(err)}")
+            del w
+
+
+def run_case_batched():
+    """One bs-64 batched step at KV 1024, replayed once inside NVTX 'replay'."""
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.batched import BatchedDecoder
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+    from llama1b_megakernel_b200.model import MegakernelLlamaForCausalLM
+
+    dev = torch.device("cuda", 0)
+    B, L = 64, 1024
+    w = syn.make_weights(cfg, seed=0, device=dev)
+    m = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=L + 64, device=dev)
+    del w
+    dec = BatchedDecoder(m, max_batch=B, max_seq_len=L + 64, page_size=64)
+    for b in range(B):
+        k, v = syn.random_kv_rows(cfg, L, seed=100 + b, seq=b, device=dev)
+        dec.kv.fill(b, k, v)
+    dec.step(syn.random_tokens(B, cfg.vocab, seed=B), torch.full((B,), L, dtype=torch.int32))
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("replay")
+    dec.replay(B)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    dec.check()
+    print("batched case done")
+
+
 def run_case_small4():
     """The ncu case: Llama-3.2-1B-shaped layers, small enough to replay (~0.7 GB)."""
     from llama1b_megakernel_b200 import synthetic as syn
@@ -509,6 +581,12 @@ def main():
     args = parse()
     if args.case == "small4":
         run_case_small4()
+        return
+    if args.case == "gemm":
+        run_case_gemm()
+        return
+    if args.case == "batched":
+        run_case_batched()
         return
     ws, rank, local = dist_init()
     try:
