@@ -496,7 +496,7 @@ def run_case_gemm():
             x[:rows] = torch.randn(rows, k, device=dev).bfloat16()
             out = torch.empty(rows, n, dtype=torch.bfloat16, device=dev)
             ws = lib.mk_gemm_workspace(n, k, rows)
-            work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+            work = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
 
             def run():
                 _lib.check(lib.mk_gemm_bf16(w.data_ptr(), n, k, x.data_ptr(), rows, bp, None,

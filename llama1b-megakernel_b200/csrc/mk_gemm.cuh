@@ -73,7 +73,8 @@ __device__ __forceinline__ uint64_t g_now() {
   return t;
 }
 
-// Bounded wait; false (and the error flag) when it runs out.
+// Bounded wait; false (and the error flag = `where`: 101 producer, 102 MMA
+// issuer, 103 epilogue) when it runs out.
 __device__ __noinline__ bool g_wait(const GemmParams& p, uint32_t bar, uint32_t parity, int where) {
   if (g_try_wait(bar, parity)) return true;
   const uint64_t t0 = g_now();
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
     int issued = 0;
     for (int i = 0; i < nk; ++i) {
       const int s = i % kGemmStages;
-      if (i >= kGemmStages && !g_wait(p, sa(&empty[s]), ((i / kGemmStages) + 1) & 1, 1)) break;
+      if (i >= kGemmStages && !g_wait(p, sa(&empty[s]), ((i / kGemmStages) + 1) & 1, 101)) break;
       const uint32_t a = ring + s * kStage, b = a + kA;
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(&full[s])),
                    "r"(kStage)
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
       const int s = i % kGemmStages;
-      if (!g_wait(p, sa(&full[s]), (i / kGemmStages) & 1, 2)) {
+      if (!g_wait(p, sa(&full[s]), (i / kGemmStages) & 1, 102)) {
         ok = false;
         break;
       }
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   __syncwarp();
 
   // ---- epilogue: warp w reads TMEM lanes 32w..32w+31 = W rows of the tile
-  const bool good = g_wait(p, sa(&done), 0, 3) && nk > 0;
+  const bool good = g_wait(p, sa(&done), 0, 103) && nk > 0;
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   float v[BP];
   tmem_ld_cols<BP>(tmem + ((uint32_t)(warp * 32) << 16), v);

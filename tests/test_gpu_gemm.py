@@ -23,7 +23,7 @@ def _run(lib, w, x, rows, residual=None, f32=False):
     dev = w.device
     out = torch.empty(rows, n, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
     ws = lib.mk_gemm_workspace(n, k, rows)
-    work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+    work = torch.zeros(max(ws, 16), dtype=torch.uint8, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     _lib.check(lib.mk_gemm_bf16(
         w.data_ptr(), n, k, x.data_ptr(), rows, bp,
@@ -65,3 +65,27 @@ def test_gemm_rejects_bad_shapes():
     rc = lib.mk_gemm_bf16(w.data_ptr(), 128, 100, x.data_ptr(), 1, 16, None, out.data_ptr(), None,
                           None, 0, err.data_ptr(), None)
     assert rc == _lib.MK_EINVAL
+
+
+def test_gemms_sharing_one_workspace():
+    """Split-K GEMMs of different shapes in sequence on one workspace (as a
+    batched step runs them): each matches its own exact sum."""
+    lib = _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    shapes = [(3072, 2048), (2048, 2048), (2048, 8192), (3072, 2048)]
+    rows, bp = 24, 32
+    ws = max(lib.mk_gemm_workspace(n, k, rows) for n, k in shapes)
+    work = torch.zeros(ws, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for n, k in shapes:
+        w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+        x = torch.zeros(bp, k, dtype=torch.bfloat16, device="cuda")
+        x[:rows] = torch.randn(rows, k, generator=g, device="cuda").bfloat16()
+        out = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+        _lib.check(lib.mk_gemm_bf16(w.data_ptr(), n, k, x.data_ptr(), rows, bp, None,
+                                    out.data_ptr(), None, work.data_ptr(), ws, err.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        exact = x[:rows].double() @ w.double().T
+        assert int(err[0]) == 0
+        assert ((out.double() - exact).abs() <= exact.abs() * 2.0 ** -7 + 1e-4).all(), (n, k)
