@@ -193,8 +193,9 @@ int mk_debug_skip_arrival(MkModel* m, int32_t cta);
  *           4 consumer ns stalled on the weight stream (cumulative),
  *           5 first copy issued, 6 producer ns stalled on a full ring
  *           (cumulative), 7 last copy issued; attention phases also
- *           8 q loaded, 9 cached chunks reduced, 10 split arrival counted,
- *           11 last split merged (for the CTA's last item).
+ *           8 q loaded, 9 cached chunks reduced, 10 warp states combined
+ *           and the output (or the split's partials) written, 11 split 0
+ *           merged the splits (for the CTA's last item).
  * buffer NULL switches tracing off; *needed (may be NULL) is set either way.
  */
 int mk_set_trace(MkModel* m, uint64_t* buffer, int64_t capacity, int64_t* needed);

@@ -27,6 +27,8 @@ namespace {
 
 thread_local std::string g_last_error;
 
+constexpr uint64_t kPartTagLimit = 0xFFFFFFFFull;  // attention partial tags stay below this
+
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -68,7 +70,9 @@ struct MkModel {
   uint32_t* attn = nullptr;
   uint32_t* act = nullptr;
   uint32_t launch_seq = 0;   // launches so far: gives each launch its own tags
-  float* partials = nullptr;
+  unsigned long long* partials = nullptr;  // attention split partials (tagged 64-bit words)
+  size_t partials_bytes = 0;
+  uint64_t part_tag_next = 0;  // partial tags used so far in the current tag sequence
   uint32_t* counters = nullptr;
   unsigned long long* keys = nullptr;
   int* error = nullptr;
@@ -308,6 +312,16 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   // 5 tagged phases per layer plus the lm_head; tags stay distinct across
   // the 65535 / (5 L + 1) launches before they repeat.
   p.tag_base = (uint32_t)(((uint64_t)m->launch_seq++ * (uint64_t)(5 * c.num_layers + 1)) % 65535u);
+  // Attention partials carry 32-bit tags of their own, one per layer and
+  // launch, so a partial block that no split wrote this launch (the split
+  // count follows the context) never matches: tags restart only after the
+  // buffer is zeroed, and 0 is never a tag.
+  if (m->part_tag_next + c.num_layers >= kPartTagLimit) {
+    MK_CUDA(cudaMemsetAsync(m->partials, 0, m->partials_bytes, static_cast<cudaStream_t>(stream)));
+    m->part_tag_next = 0;
+  }
+  p.part_tag0 = (uint32_t)(1 + m->part_tag_next);
+  m->part_tag_next += c.num_layers;
   p.trace = m->trace;
   p.trace_per_cta = (c.num_layers * 5 + 1) * mk::kTraceKinds;
   p.tp_rank = m->tp_rank;
@@ -338,6 +352,7 @@ constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_ptr[kStaticMaxDevices] = {};  // device address of g_static_scratch, per device
 uint32_t g_static_seq[kStaticMaxDevices] = {};  // launches so far per device (tags, see enqueue)
+uint64_t g_static_part[kStaticMaxDevices] = {};  // partial tags used per device (see enqueue)
 
 // Once per device, with that device current: the array's device address (the
 // host-side name g_static_scratch is only a stand-in and must never reach a
@@ -530,8 +545,9 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 4);
   const size_t o_attn = take(B * NQ * 64 * 4);
   const size_t o_act = take(B * I * 4);
-  const size_t o_part = take(B * NKV * mk::kMaxSplit * mk::kGroup * mk::kPartialStride * 4);
-  const size_t o_cnt = take((mk::kCntArrive + B * NKV) * 4);
+  const size_t part_bytes = (size_t)m->grid * mk::kGroup * mk::kPartialStride * 8;
+  const size_t o_part = take(part_bytes);
+  const size_t o_cnt = take(mk::kCounters * 4);
   const size_t o_keys = take(B * 8);
   const size_t o_err = take(16);
   m->counters_bytes = o_err + 256 - o_cnt;  // counters, keys and error word
@@ -547,7 +563,8 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   m->qkv = reinterpret_cast<uint32_t*>(cb + o_qkv);
   m->attn = reinterpret_cast<uint32_t*>(cb + o_attn);
   m->act = reinterpret_cast<uint32_t*>(cb + o_act);
-  m->partials = reinterpret_cast<float*>(cb + o_part);
+  m->partials = reinterpret_cast<unsigned long long*>(cb + o_part);
+  m->partials_bytes = part_bytes;
   m->counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
   m->keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
   m->error = reinterpret_cast<int*>(cb + o_err);
@@ -642,8 +659,9 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   const size_t o_qkv = take(B * (NQ + 2 * NKV) * 64 * 4);
   const size_t o_attn = take(B * NQ * 64 * 4);
   const size_t o_act = take(B * I * 4);
-  const size_t o_part = take(B * NKV * mk::kMaxSplit * mk::kGroup * mk::kPartialStride * 4);
-  const size_t o_cnt = take((mk::kCntArrive + B * NKV) * 4);
+  const size_t part_bytes = (size_t)sms * mk::kGroup * mk::kPartialStride * 8;
+  const size_t o_part = take(part_bytes);
+  const size_t o_cnt = take(mk::kCounters * 4);
   const size_t o_keys = take(B * 8);
   const size_t o_err = take(16);
   const size_t o_mirror = take(16);
@@ -661,7 +679,8 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   m.qkv = reinterpret_cast<uint32_t*>(cb + o_qkv);
   m.attn = reinterpret_cast<uint32_t*>(cb + o_attn);
   m.act = reinterpret_cast<uint32_t*>(cb + o_act);
-  m.partials = reinterpret_cast<float*>(cb + o_part);
+  m.partials = reinterpret_cast<unsigned long long*>(cb + o_part);
+  m.partials_bytes = part_bytes;
   m.counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
   m.keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
   m.error = reinterpret_cast<int*>(cb + o_err);
@@ -670,14 +689,23 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   m.host_error_dev = error_out ? reinterpret_cast<int*>(error_out) : reinterpret_cast<int*>(cb + o_mirror);
   rc = mk_load_weights(&m, w);
   if (rc) return rc;
+  bool restart = false;
   {
     std::lock_guard<std::mutex> lock(g_static_mu);
     m.launch_seq = g_static_seq[device]++;
+    m.part_tag_next = g_static_part[device];
+    if (m.part_tag_next + cfg->num_layers >= kPartTagLimit) {
+      m.part_tag_next = 0;
+      restart = true;
+    }
+    g_static_part[device] = m.part_tag_next + cfg->num_layers;
   }
 
-  // What must start at zero: barrier and arrival counters, argmax keys and
-  // error words (a previous call that failed on the device leaves them set).
+  // What must start at zero: barrier counters, argmax keys and error words
+  // (a previous call that failed on the device leaves them set), and the
+  // partials when their tag sequence restarts.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (restart) MK_CUDA(cudaMemsetAsync(m.partials, 0, m.partials_bytes, st));
   MK_CUDA(cudaMemsetAsync(cb + o_cnt, 0, o_mirror + 16 - o_cnt, st));
   if (error_out) MK_CUDA(cudaMemsetAsync(error_out, 0, 4 * sizeof(int32_t), st));
   return enqueue(&m, 0, tokens, positions, batch, kv, nullptr, nullptr, logits, next_ids, flags,

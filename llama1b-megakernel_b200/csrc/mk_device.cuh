@@ -54,8 +54,8 @@ enum DevErr : int {
 
 // Counters in the scratch counter block.
 enum Counter : int {
-  kCntDone = 2,    // CTAs finished with the step (the last publishes the argmax)
-  kCntArrive = 4,  // + b * nkv + g: attention splits finished per (sequence, kv head)
+  kCntDone = 2,  // CTAs finished with the step (the last publishes the argmax)
+  kCounters = 4,  // words in the counter block
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

@@ -93,7 +93,9 @@ struct Params {
   uint32_t* qkv;   // [B][NQ + 2 NKV][64]
   uint32_t* attn;  // [B][NQ * 64]
   uint32_t* act;   // [B][I]
-  float* partials; // [B][NKV][kMaxSplit][kGroup][kPartialStride]
+  // Attention split partials, one block per attention item (< grid when
+  // split): [item][kGroup][kPartialStride] words of part_tag << 32 | fp32.
+  unsigned long long* partials;
   uint32_t* counters;
   unsigned long long* keys;  // [B]
   int* error;                // [4] code, detail, cta, thread (device)
@@ -101,6 +103,8 @@ struct Params {
   unsigned long long timeout_ns;
   int debug_skip_cta;
   uint32_t tag_base;  // this launch's first tag (consecutive launches use disjoint tags)
+  uint32_t part_tag0;  // layer 0's partial tag (layer l: + l); never 0, unique until the
+                       // host zeroes the partials and restarts the sequence
   // optional phase trace ([grid][trace_per_cta] u64, see kTrace*); nullptr = off
   unsigned long long* trace;
   int trace_per_cta;
@@ -142,8 +146,8 @@ enum TraceKind : int {
   kTrProdEnd = 7,      // producer issued the phase's last copy
   kTrAttnQ = 8,        // attention: q / new K,V loaded (last item of the CTA)
   kTrAttnChunks = 9,   // attention: cached chunks reduced
-  kTrAttnArrive = 10,  // attention: split partials written, arrival counted
-  kTrAttnMerged = 11,  // attention: last split merged and published (if last)
+  kTrAttnArrive = 10,  // attention: warp states combined, output or split partials written
+  kTrAttnMerged = 11,  // attention: split 0 merged the splits and published (if split)
   kTraceKinds = 12,
 };
 
@@ -232,6 +236,46 @@ struct Polled {
   uint4 u;
   int ok;
 };
+
+// A 64-bit tagged word: tag << 32 | fp32 bits (one single-copy-atomic store).
+__device__ __forceinline__ unsigned long long tagged64(float v, uint32_t tag) {
+  return ((unsigned long long)tag << 32) | __float_as_uint(v);
+}
+
+struct Polled64 {
+  unsigned long long v;
+  int ok;
+};
+
+// Spin (bounded) until the 64-bit word at src carries `tag`.
+__device__ __noinline__ Polled64 poll_tagged64_slow(const Params& p, const unsigned long long* src,
+                                                    uint32_t tag, int where) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    const unsigned long long v = __ldcg(src);
+    if ((uint32_t)(v >> 32) == tag) return {v, 1};
+    if ((it & 15) == 0) {
+      if (aborted(p)) return {v, 0};
+      if (global_ns() - t0 > p.timeout_ns) {
+        raise_error(p, kErrBarrierTimeout, where);
+        return {v, 0};
+      }
+    }
+  }
+}
+
+// The fp32 value of a 64-bit word already loaded as v, polled at src until it
+// carries `tag` if it did not yet. false on abort or timeout.
+__device__ __forceinline__ bool value64(const Params& p, const unsigned long long* src,
+                                        unsigned long long v, uint32_t tag, float& out, int where) {
+  if ((uint32_t)(v >> 32) != tag) {
+    const Polled64 r = poll_tagged64_slow(p, src, tag, where);
+    if (!r.ok) return false;
+    v = r.v;
+  }
+  out = __uint_as_float((uint32_t)v);
+  return true;
+}
 
 // Slow path of poll_tagged: re-read until the tags match (time-bounded). No
 // sleep between reads: the wait is on the step's critical path (a 64 ns
@@ -964,49 +1008,77 @@ __device__ __noinline__ bool gemv_phase(const Params& p, Ring& ring_io, uint32_t
 
 
 static_assert(kConsumerThreads >= kGroup * kHeadDim + kGroup * kMaxSplit,
-              "merge_group needs a thread per (head, dim) plus one per (head, split)");
+              "merge_splits needs a thread per (head, dim) plus one per (head, split)");
 static_assert(kGroup * kMaxSplit * 2 <= kAttnWarps * kGroup * kPartialStride,
-              "merge_group keeps its (m, l) table in the attention scratch");
+              "merge_splits keeps its (m, l) table in the attention scratch");
 
-// The last split to finish a (seq b, kv head g) merges every split's
-// (m, l, o) — split 0 already holds the new token's own K/V — and writes the
-// group's bf16 head outputs. All consumer threads call it. The per-split
-// loads are issued before any is used, so the merge costs one L2 round trip.
-__device__ __noinline__ void merge_group(const Params& p, int b, int g, int ns, float* ml,
-                                         uint32_t tag) {
+// Split 0 of a (seq b, kv head g) merges the other splits' tagged (o, m, l)
+// partials (blocks base + s * kGroup * kPartialStride, s = 1 .. ns - 1) with
+// its own state — thread hh * 64 + d holds (O0, M0, L0) of head hh, dim d,
+// and split 0 holds the new token's own K/V, so L0 > 0 — and writes the
+// group's tagged bf16 head outputs to `out`. The merge is
+//   M = max_s m_s,  o = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s
+// summed in split order. Every load is issued before any is used; a word
+// whose tag is not yet there is polled (bounded). All consumer threads call
+// it; false on abort or timeout.
+__device__ __noinline__ bool merge_splits(const Params& p, const unsigned long long* base, int ns,
+                                          float O0, float M0, float L0, float* ml, uint32_t ptag,
+                                          uint32_t* out, uint32_t otag, int where) {
+  constexpr int kChunk = 4;  // o loads in flight per thread
   const int tid = threadIdx.x;
-  const float* base = p.partials + ((size_t)b * p.NKV + g) * kMaxSplit * kGroup * kPartialStride;
   const bool worker = tid < kGroup * kHeadDim;
   const int hh = (tid >> 6) & (kGroup - 1), d = tid & 63;
-  float os[kMaxSplit];
+  const size_t step = (size_t)kGroup * kPartialStride;
+  const unsigned long long* ob = base + hh * kPartialStride + d;  // split s: ob + s * step
+  unsigned long long v[kChunk];
+  bool ok = true;
   if (worker) {
 #pragma unroll
-    for (int s = 0; s < kMaxSplit; ++s)
-      if (s < ns) os[s] = __ldcg(base + (size_t)(s * kGroup + hh) * kPartialStride + d);
-  } else if (tid < kGroup * kHeadDim + kGroup * ns) {
-    const int i = tid - kGroup * kHeadDim, h2 = i / ns, s = i % ns;
-    const float* ps = base + (size_t)(s * kGroup + h2) * kPartialStride;
-    ml[(h2 * kMaxSplit + s) * 2] = __ldcg(ps + kHeadDim);
-    ml[(h2 * kMaxSplit + s) * 2 + 1] = __ldcg(ps + kHeadDim + 1);
+    for (int j = 0; j < kChunk; ++j)
+      if (1 + j < ns) v[j] = __ldcg(ob + (1 + j) * step);
+  } else if (tid < kGroup * kHeadDim + kGroup * (ns - 1)) {
+    const int i = tid - kGroup * kHeadDim, h2 = i / (ns - 1), s = 1 + i % (ns - 1);
+    const unsigned long long* w = base + s * step + h2 * kPartialStride + kHeadDim;
+    const unsigned long long vm = __ldcg(w), vl = __ldcg(w + 1);
+    float m = 0.f, l = 0.f;
+    ok = value64(p, w, vm, ptag, m, where) && value64(p, w + 1, vl, ptag, l, where);
+    ml[(h2 * kMaxSplit + s) * 2] = m;
+    ml[(h2 * kMaxSplit + s) * 2 + 1] = l;
   }
-  consumer_sync();
+  if (consumer_any(!ok)) return false;  // also the barrier before ml is read
   if (worker) {
     const float* mh = ml + hh * kMaxSplit * 2;
-    float M = -INFINITY;
-#pragma unroll
-    for (int s = 0; s < kMaxSplit; ++s)
-      if (s < ns) M = fmaxf(M, mh[2 * s]);
+    float M = M0;
+    for (int s = 1; s < ns; ++s) M = fmaxf(M, mh[2 * s]);
     float L = 0.f, O = 0.f;
+    if (M0 > -INFINITY) {
+      const float f = __expf(M0 - M);
+      L += f * L0;
+      O += f * O0;
+    }
+    for (int s0 = 1; s0 < ns && ok; s0 += kChunk) {
+      if (s0 > 1) {
 #pragma unroll
-    for (int s = 0; s < kMaxSplit; ++s) {
-      if (s < ns && mh[2 * s] > -INFINITY) {
-        const float f = __expf(mh[2 * s] - M);
-        L += f * mh[2 * s + 1];
-        O += f * os[s];
+        for (int j = 0; j < kChunk; ++j)
+          if (s0 + j < ns) v[j] = __ldcg(ob + (s0 + j) * step);
+      }
+#pragma unroll
+      for (int j = 0; j < kChunk; ++j) {
+        if (s0 + j < ns && ok) {
+          float o = 0.f;
+          ok = value64(p, ob + (s0 + j) * step, v[j], ptag, o, where);
+          const float m = mh[2 * (s0 + j)];
+          if (m > -INFINITY) {
+            const float f = __expf(m - M);
+            L += f * mh[2 * (s0 + j) + 1];
+            O += f * o;
+          }
+        }
       }
     }
-    p.attn[(size_t)b * p.NQ * kHeadDim + (g * kGroup + hh) * kHeadDim + d] = tagged(O / L, tag);
+    if (ok) out[hh * kHeadDim + d] = tagged(O / L, otag);
   }
+  return !consumer_any(!ok);
 }
 
 // Online-softmax merge of another (m, l, o[8]) state into this lane's.
@@ -1184,6 +1256,7 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
     consumer_sync();
     static_assert(kConsumerWarps >= kAttnWarps && kConsumerWarps <= 2 * kAttnWarps,
                   "attention merge assumes kAttnWarps <= warps <= 2 * kAttnWarps");
+    float O0 = 0.f, M0 = -INFINITY, L0 = 0.f;  // split 0's state, for merge_splits
     if (tid < kGroup * kHeadDim) {
       const int hh = tid >> 6, d = tid & 63;
       float M = -INFINITY;
@@ -1207,36 +1280,31 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
         // The only split (it holds the active slot, so L > 0): final output.
         p.attn[(size_t)a.b * p.NQ * kHeadDim + (a.g * kGroup + hh) * kHeadDim + d] =
             tagged(O / L, phase_tag(p, layer * 5 + 1));
-      } else {
-        float* pp2 = p.partials +
-                     ((((size_t)a.b * p.NKV + a.g) * kMaxSplit + a.s) * kGroup + hh) * kPartialStride;
-        pp2[d] = O;
+      } else if (a.s != 0) {
+        // Publish this split's partial state; split 0 merges.
+        unsigned long long* pp2 = p.partials + ((size_t)it * kGroup + hh) * kPartialStride;
+        const uint32_t ptag = p.part_tag0 + (uint32_t)layer;
+        pp2[d] = tagged64(O, ptag);
         if (d == 0) {
-          pp2[kHeadDim] = M;
-          pp2[kHeadDim + 1] = L;
+          pp2[kHeadDim] = tagged64(M, ptag);
+          pp2[kHeadDim + 1] = tagged64(L, ptag);
         }
+      } else {
+        O0 = O;
+        M0 = M;
+        L0 = L;
       }
     }
-    if (ns == 1) {
-      // The tagged outputs are the publication.
-      if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
-      continue;
-    }
-    consumer_sync();
-    // Count the split; the last one of its (seq, kv head) merges them all.
-    if (tid == 0) {
-      uint32_t* arr = p.counters + kCntArrive + a.b * p.NKV + a.g;
-      const uint32_t old = atom_add_acq_rel_u32(arr, 1u);
-      const int last = (old == (uint32_t)(ns - 1)) ? 1 : 0;
-      if (last) atomicExch(arr, 0u);
-      st.flag = last;
-      if (p.trace) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
-    }
-    consumer_sync();
-    if (st.flag) {
-      merge_group(p, a.b, a.g, ns, comb, phase_tag(p, layer * 5 + 1));
-      if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnMerged, global_ns());
-    }
+    if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
+    if (ns == 1 || a.s != 0) continue;  // the tagged words written above are the publication
+    consumer_sync();  // every thread is done reading the warp states in comb
+    if (!merge_splits(p, p.partials + (size_t)it * kGroup * kPartialStride, ns, O0, M0, L0, comb,
+                      p.part_tag0 + (uint32_t)layer,
+                      p.attn + (size_t)a.b * p.NQ * kHeadDim + a.g * kGroup * kHeadDim,
+                      phase_tag(p, layer * 5 + 1), 3100 + layer))
+      return false;
+    if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnMerged, global_ns());
+    break;  // with ns > 1 a CTA has one item at most (T <= grid)
   }
   return true;
 }

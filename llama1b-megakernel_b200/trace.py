@@ -73,8 +73,8 @@ def format_table(summary: dict) -> str:
 
 def attention_breakdown(trace, num_layers: int) -> dict:
     """Attention sub-steps (us, mean over layers 1..L-1 of the median / max
-    over the CTAs that had an item): q load, chunk reduction, split
-    arrival, and the last split's merge."""
+    over the CTAs that had an item): q load, chunk reduction, the warp
+    states' combine and publication, and split 0's merge of the splits."""
     t = np.asarray(trace, dtype=np.int64).astype(np.float64)
     keys = {"q_load": (WAIT_DONE, ATTN_Q), "chunks": (ATTN_Q, ATTN_CHUNKS),
             "arrive": (ATTN_CHUNKS, ATTN_ARRIVE), "merge": (ATTN_ARRIVE, ATTN_MERGED)}
