@@ -444,7 +444,7 @@ def run_ours(args, ws, rank, local):
 def run_batched(model, cfg, dev, hbm_peak):
     """bs 8, 32, 64, one greedy step at KV length 1024 per
     sequence (independent seeded N(0,1) caches, random tokens), through the
-    batched path (batched.py: paged attention kernel + cuBLAS projections, one
+    batched path (batched.py: paged attention kernel + tcgen05 projections, one
     CUDA graph per batch size). Step time = median of 20 graph replays."""
     from llama1b_megakernel_b200 import synthetic as syn
     from llama1b_megakernel_b200.batched import BatchedDecoder
@@ -473,7 +473,7 @@ def run_batched(model, cfg, dev, hbm_peak):
         res[str(B)] = {"ms_p50": med, "tok_s": B * 1e3 / med, "bytes_per_step": byts,
                        "achieved_gbs": byts / (med / 1e3) / 1e9,
                        "frac_of_peak": byts / (med / 1e3) / 1e9 / hbm_peak,
-                       "gemm": "cuBLAS (torch F.linear)", "attention": "mk_paged_attention"}
+                       "gemm": "mk_gemm_bf16 (tcgen05)", "attention": "mk_paged_attention"}
     del dec
     torch.cuda.empty_cache()
     return res
