@@ -14,9 +14,10 @@
 //    shared buffers while it computes the current one, whose pieces are
 //    XOR-swizzled by row so both products read shared memory without bank
 //    conflicts;
-//  * scores: lane (r, h) dots q head h (packed bf16 in registers,
-//    fma.rn.f32.bf16) with rows r, r+8, r+16, r+24; P . V: lane j owns dims
-//    2j, 2j+1 of all 32 rows for the 4 heads;
+//  * both products on the tensor cores (mma.sync m16n8k16, bf16 inputs, fp32
+//    accumulation): scores with the 4 q heads as the rows of the A tile and
+//    K from ldmatrix, P . V with P (rounded to bf16, as flash attention does)
+//    taken straight from the score accumulators and V from ldmatrix.trans;
 //  * online softmax in fp32 per head; the CTA's warps are merged in shared
 //    memory, and the CTA writes one (m, l, o[64]) partial per head;
 //  * a merge kernel (one CTA per sequence and kv head) combines the splits and
@@ -34,6 +35,7 @@ namespace mk {
 constexpr int kAttnCtaWarps = 4;
 constexpr int kAttnPartial = 2 + 64;  // m, l, o[64]
 constexpr int kAttnChunkBytes = 32 * 128;  // 32 rows of K (or V)
+constexpr int kAttnPageCache = 128;        // page ids of a split kept in shared memory
 // Shared memory per CTA: per warp two chunk buffers of K and V.
 constexpr int kAttnSmem = kAttnCtaWarps * 2 * 2 * kAttnChunkBytes;
 
@@ -50,22 +52,6 @@ struct PagedAttnParams {
   int* error;
 };
 
-__device__ __forceinline__ float2 bf2x2(uint32_t w) {
-  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-}
-
-// c0 += lo(a) lo(b), c1 += hi(a) hi(b) on packed bf16 pairs, in fp32 (the
-// products of two bf16 values are exact in fp32).
-__device__ __forceinline__ void attn_fma2(uint32_t a, uint32_t b, float& c0, float& c1) {
-  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
-      "mov.b32 {al, ah}, %2;\n\t"
-      "mov.b32 {bl, bh}, %3;\n\t"
-      "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
-      "fma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
-      : "+f"(c0), "+f"(c1)
-      : "r"(a), "r"(b));
-}
-
 // 16-byte asynchronous copy global -> shared; src_bytes 0 fills zeros.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
@@ -79,18 +65,24 @@ __device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((c ^ (
 
 __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __grid_constant__ PagedAttnParams p) {
   extern __shared__ __align__(128) uint8_t asmem[];
-  __shared__ float pw[kAttnCtaWarps][4][32];               // probabilities of a chunk
   __shared__ float st[kAttnCtaWarps][4][kAttnPartial];     // per-warp states
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // scores: lane = (position r8 of each 8, head h); P . V: lane = dims 2 lane, 2 lane + 1
-  const int h = lane & 3, r8 = lane >> 2;
   const int len = p.lengths[b];
   const int p0 = s * p.split_len, p1 = min(len, p0 + p.split_len);
   const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(asmem) + warp * 4 * kAttnChunkBytes;
   // buffer j (0, 1): K at wbuf + j * 2 * kAttnChunkBytes, V right after it
   const int* table = p.block_tables + (size_t)b * p.max_blocks;
   const int nchunks = p1 > p0 ? (p1 - p0 + 31) / 32 : 0;
+  // The split's page ids, staged in shared memory once (when they fit), so
+  // issuing a chunk's copies waits on no global load.
+  __shared__ int pages_s[kAttnPageCache];
+  const int blk0 = p0 / p.ps;
+  const int nblk = p1 > p0 ? (p1 - 1) / p.ps - blk0 + 1 : 0;
+  const bool staged = nblk <= kAttnPageCache;
+  if (staged)
+    for (int i = threadIdx.x; i < nblk; i += kAttnCtaWarps * 32) pages_s[i] = table[blk0 + i];
+  __syncthreads();
   // this warp takes chunks warp, warp + 4, ... of the split
   auto issue = [&](int ci, int j) {
     const int c0 = p0 + ci * 32;
@@ -102,7 +94,7 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
       const __nv_bfloat16* vs = p.v;
       uint32_t bytes = 0;
       if (pos < p1) {
-        const int page = table[pos / p.ps];
+        const int page = staged ? pages_s[pos / p.ps - blk0] : table[pos / p.ps];
         if (page >= 0 && page < p.num_pages) {
           const size_t off = (((size_t)page * p.NKV + g) * p.ps + pos % p.ps) * 64 + piece * 8;
           ks += off;
@@ -118,23 +110,30 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
-  // q head h as packed bf16 (the scale is applied to the fp32 score)
-  uint32_t q[32];
+  // Tensor cores (mma.m16n8k16, bf16 in, fp32 accumulate). Scores: S = Q K^T
+  // with Q as the A tile (rows 0..3 the group's q heads, rows 4..15 zero)
+  // and 8 positions of K per B tile, loaded from the swizzled rows with
+  // ldmatrix; lane (g = lane / 4, t = lane % 4) then holds the scores of head
+  // g (if g < 4) at positions 8 nb + 2 t, + 1. P . V: the scores' accumulator
+  // layout is the A layout of P (16 positions per k step, P rounded to bf16)
+  // and V comes in with ldmatrix.trans; O rows 0..3 are the heads, lane
+  // (g, t) holds dims 8 db + 2 t, + 1 of head g in o[db].
+  const int g8 = lane >> 2, t4 = lane & 3;
+  uint32_t qa[4][2];  // k step kk: dims 16 kk + 2 t4 (+1) and 16 kk + 8 + 2 t4 (+1) of head g8
   {
-    const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.NQ + g * 4 + h) * 64);
+    const __nv_bfloat16* qh = p.q + ((size_t)b * p.NQ + g * 4 + (g8 & 3)) * 64;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint4 u = __ldg(qp + c);
-      q[c * 4 + 0] = u.x;
-      q[c * 4 + 1] = u.y;
-      q[c * 4 + 2] = u.z;
-      q[c * 4 + 3] = u.w;
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t lo = __ldg(reinterpret_cast<const uint32_t*>(qh + 16 * kk + 2 * t4));
+      const uint32_t hi = __ldg(reinterpret_cast<const uint32_t*>(qh + 16 * kk + 8 + 2 * t4));
+      qa[kk][0] = g8 < 4 ? lo : 0u;
+      qa[kk][1] = g8 < 4 ? hi : 0u;
     }
   }
-  float m = -INFINITY, l = 0.f;  // head h's running max and sum (same in its 8 lanes)
-  float o[4][2];
+  float m = -INFINITY, l = 0.f;  // head g8's running max and sum (same in its 4 lanes)
+  float o[8][4];
 #pragma unroll
-  for (int hh = 0; hh < 4; ++hh) o[hh][0] = o[hh][1] = 0.f;
+  for (int db = 0; db < 8; ++db) o[db][0] = o[db][1] = o[db][2] = o[db][3] = 0.f;
 
   int j = 0;
   if (warp < nchunks) issue(warp, 0);
@@ -148,77 +147,95 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
     __syncwarp();
     const int c0 = p0 + ci * 32;
     const uint32_t kb = wbuf + j * 2 * kAttnChunkBytes, vb = kb + kAttnChunkBytes;
-    // ---- scores from shared memory
-    float sc[4];
+    // ---- scores: four blocks of 8 positions
+    float sc[4][4];
     float cm = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int row = r * 8 + r8;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int nb = 0; nb < 4; ++nb) {
+      sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 u;
-        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
-                     : "r"(kb + swz(row, c)));
-        attn_fma2(u.x, q[c * 4 + 0], a0, a1);
-        attn_fma2(u.y, q[c * 4 + 1], a2, a3);
-        attn_fma2(u.z, q[c * 4 + 2], a0, a1);
-        attn_fma2(u.w, q[c * 4 + 3], a2, a3);
+      for (int half = 0; half < 2; ++half) {  // pieces 4 half .. 4 half + 3 = k steps 2 half, 2 half + 1
+        uint32_t kf[4];
+        const uint32_t addr = kb + swz(nb * 8 + (lane & 7), half * 4 + (lane >> 3));
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(kf[0]), "=r"(kf[1]), "=r"(kf[2]), "=r"(kf[3])
+                     : "r"(addr));
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int kk = half * 2 + u;
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+              "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+              : "+f"(sc[nb][0]), "+f"(sc[nb][1]), "+f"(sc[nb][2]), "+f"(sc[nb][3])
+              : "r"(qa[kk][0]), "r"(0u), "r"(qa[kk][1]), "r"(0u), "r"(kf[2 * u]), "r"(kf[2 * u + 1]));
+        }
       }
-      const int pos = c0 + row;
-      sc[r] = pos < p1 ? ((a0 + a1) + (a2 + a3)) * p.scale : -INFINITY;
-      cm = fmaxf(cm, sc[r]);
-    }
-    // head h's max and sum over the chunk: its 8 lanes differ in lane bits 2..4
 #pragma unroll
-    for (int d = 4; d < 32; d <<= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, d));
+      for (int e = 0; e < 2; ++e) {
+        const int pos = c0 + nb * 8 + 2 * t4 + e;
+        sc[nb][e] = pos < p1 ? sc[nb][e] * p.scale : -INFINITY;
+        cm = fmaxf(cm, sc[nb][e]);
+      }
+    }
+    // head g8's max and sum over the chunk: its 4 lanes differ in lane bits 0..1
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
     const float mn = fmaxf(m, cm);
     const float alpha = (mn == -INFINITY) ? 1.f : __expf(m - mn);
     float sum = 0.f;
+    uint32_t pa[4];  // P as bf16 pairs: block nb, positions 8 nb + 2 t4, + 1
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float e = (sc[r] == -INFINITY) ? 0.f : __expf(sc[r] - mn);
-      pw[warp][h][r * 8 + r8] = e;
-      sum += e;
+    for (int nb = 0; nb < 4; ++nb) {
+      const float e0 = (sc[nb][0] == -INFINITY) ? 0.f : __expf(sc[nb][0] - mn);
+      const float e1 = (sc[nb][1] == -INFINITY) ? 0.f : __expf(sc[nb][1] - mn);
+      sum += e0 + e1;
+      __nv_bfloat162 pr = __floats2bfloat162_rn(e0, e1);
+      pa[nb] = *reinterpret_cast<uint32_t*>(&pr);
     }
-#pragma unroll
-    for (int d = 4; d < 32; d <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     l = l * alpha + sum;
     m = mn;
-    __syncwarp();
-    // ---- P . V from shared memory
 #pragma unroll
-    for (int hh = 0; hh < 4; ++hh) {
-      const float a = __shfl_sync(0xffffffffu, alpha, hh);  // lane hh holds head hh
-      o[hh][0] *= a;
-      o[hh][1] *= a;
+    for (int db = 0; db < 8; ++db) {
+      o[db][0] *= alpha;
+      o[db][1] *= alpha;
     }
-    const int n = min(32, p1 - c0);
-    for (int jj = 0; jj < n; ++jj) {
-      uint32_t vw;
-      asm volatile("ld.shared.u32 %0, [%1];"
-                   : "=r"(vw)
-                   : "r"(vb + swz(jj, lane >> 2) + (lane & 3) * 4));
-      const float2 f = bf2x2(vw);
+    // ---- P . V: two k steps of 16 positions, eight blocks of 8 dims
 #pragma unroll
-      for (int hh = 0; hh < 4; ++hh) {
-        const float pr = pw[warp][hh][jj];
-        o[hh][0] = fmaf(pr, f.x, o[hh][0]);
-        o[hh][1] = fmaf(pr, f.y, o[hh][1]);
+    for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+      for (int dp = 0; dp < 4; ++dp) {  // dim pieces 2 dp, 2 dp + 1
+        uint32_t vf[4];
+        const int row = ks * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+        const uint32_t addr = vb + swz(row, dp * 2 + (lane >> 4));
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(vf[0]), "=r"(vf[1]), "=r"(vf[2]), "=r"(vf[3])
+                     : "r"(addr));
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int db = dp * 2 + u;
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+              "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+              : "+f"(o[db][0]), "+f"(o[db][1]), "+f"(o[db][2]), "+f"(o[db][3])
+              : "r"(pa[2 * ks]), "r"(0u), "r"(pa[2 * ks + 1]), "r"(0u), "r"(vf[2 * u]), "r"(vf[2 * u + 1]));
+        }
       }
     }
     __syncwarp();
   }
   // ---- merge the warps, write the CTA's partial per head
-  if (lane < 4) {
-    st[warp][h][0] = m;
-    st[warp][h][1] = l;
-  }
+  if (g8 < 4) {
+    if (t4 == 0) {
+      st[warp][g8][0] = m;
+      st[warp][g8][1] = l;
+    }
 #pragma unroll
-  for (int hh = 0; hh < 4; ++hh) {
-    st[warp][hh][2 + 2 * lane] = o[hh][0];
-    st[warp][hh][3 + 2 * lane] = o[hh][1];
+    for (int db = 0; db < 8; ++db) {
+      st[warp][g8][2 + db * 8 + 2 * t4] = o[db][0];
+      st[warp][g8][3 + db * 8 + 2 * t4] = o[db][1];
+    }
   }
   __syncthreads();
   float* dst = p.work + ((((size_t)b * p.NKV + g) * p.splits + s) * 4) * kAttnPartial;

@@ -1012,18 +1012,17 @@ static_assert(kConsumerThreads >= kGroup * kHeadDim + kGroup * kMaxSplit,
 static_assert(kGroup * kMaxSplit * 2 <= kAttnWarps * kGroup * kPartialStride,
               "merge_splits keeps its (m, l) table in the attention scratch");
 
-// Split 0 of a (seq b, kv head g) merges the other splits' tagged (o, m, l)
-// partials (blocks base + s * kGroup * kPartialStride, s = 1 .. ns - 1) with
-// its own state — thread hh * 64 + d holds (O0, M0, L0) of head hh, dim d,
-// and split 0 holds the new token's own K/V, so L0 > 0 — and writes the
-// group's tagged bf16 head outputs to `out`. The merge is
+// Split 0 of a (seq b, kv head g) merges the tagged (o, m, l) partials of
+// all ns splits (blocks base + s * kGroup * kPartialStride; split 0 holds the
+// new token's own K/V, so the sum of l is > 0) and writes the group's tagged
+// bf16 head outputs to `out`. The merge is
 //   M = max_s m_s,  o = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s
 // summed in split order. Every load is issued before any is used; a word
 // whose tag is not yet there is polled (bounded). All consumer threads call
 // it; false on abort or timeout.
 __device__ __noinline__ bool merge_splits(const Params& p, const unsigned long long* base, int ns,
-                                          float O0, float M0, float L0, float* ml, uint32_t ptag,
-                                          uint32_t* out, uint32_t otag, int where) {
+                                          float* ml, uint32_t ptag, uint32_t* out, uint32_t otag,
+                                          int where) {
   constexpr int kChunk = 4;  // o loads in flight per thread
   const int tid = threadIdx.x;
   const bool worker = tid < kGroup * kHeadDim;
@@ -1035,9 +1034,9 @@ __device__ __noinline__ bool merge_splits(const Params& p, const unsigned long l
   if (worker) {
 #pragma unroll
     for (int j = 0; j < kChunk; ++j)
-      if (1 + j < ns) v[j] = __ldcg(ob + (1 + j) * step);
-  } else if (tid < kGroup * kHeadDim + kGroup * (ns - 1)) {
-    const int i = tid - kGroup * kHeadDim, h2 = i / (ns - 1), s = 1 + i % (ns - 1);
+      if (j < ns) v[j] = __ldcg(ob + j * step);
+  } else if (tid < kGroup * kHeadDim + kGroup * ns) {
+    const int i = tid - kGroup * kHeadDim, h2 = i / ns, s = i % ns;
     const unsigned long long* w = base + s * step + h2 * kPartialStride + kHeadDim;
     const unsigned long long vm = __ldcg(w), vl = __ldcg(w + 1);
     float m = 0.f, l = 0.f;
@@ -1048,16 +1047,11 @@ __device__ __noinline__ bool merge_splits(const Params& p, const unsigned long l
   if (consumer_any(!ok)) return false;  // also the barrier before ml is read
   if (worker) {
     const float* mh = ml + hh * kMaxSplit * 2;
-    float M = M0;
-    for (int s = 1; s < ns; ++s) M = fmaxf(M, mh[2 * s]);
+    float M = -INFINITY;
+    for (int s = 0; s < ns; ++s) M = fmaxf(M, mh[2 * s]);
     float L = 0.f, O = 0.f;
-    if (M0 > -INFINITY) {
-      const float f = __expf(M0 - M);
-      L += f * L0;
-      O += f * O0;
-    }
-    for (int s0 = 1; s0 < ns && ok; s0 += kChunk) {
-      if (s0 > 1) {
+    for (int s0 = 0; s0 < ns && ok; s0 += kChunk) {
+      if (s0 > 0) {
 #pragma unroll
         for (int j = 0; j < kChunk; ++j)
           if (s0 + j < ns) v[j] = __ldcg(ob + (s0 + j) * step);
@@ -1256,7 +1250,6 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
     consumer_sync();
     static_assert(kConsumerWarps >= kAttnWarps && kConsumerWarps <= 2 * kAttnWarps,
                   "attention merge assumes kAttnWarps <= warps <= 2 * kAttnWarps");
-    float O0 = 0.f, M0 = -INFINITY, L0 = 0.f;  // split 0's state, for merge_splits
     if (tid < kGroup * kHeadDim) {
       const int hh = tid >> 6, d = tid & 63;
       float M = -INFINITY;
@@ -1280,7 +1273,7 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
         // The only split (it holds the active slot, so L > 0): final output.
         p.attn[(size_t)a.b * p.NQ * kHeadDim + (a.g * kGroup + hh) * kHeadDim + d] =
             tagged(O / L, phase_tag(p, layer * 5 + 1));
-      } else if (a.s != 0) {
+      } else {
         // Publish this split's partial state; split 0 merges.
         unsigned long long* pp2 = p.partials + ((size_t)it * kGroup + hh) * kPartialStride;
         const uint32_t ptag = p.part_tag0 + (uint32_t)layer;
@@ -1289,16 +1282,12 @@ __device__ __noinline__ bool attention_phase(const Params& p, Ring& ring_io, Sme
           pp2[kHeadDim] = tagged64(M, ptag);
           pp2[kHeadDim + 1] = tagged64(L, ptag);
         }
-      } else {
-        O0 = O;
-        M0 = M;
-        L0 = L;
       }
     }
     if (p.trace && tid == 0) trace_put(p, layer * 5 + 1, kTrAttnArrive, global_ns());
     if (ns == 1 || a.s != 0) continue;  // the tagged words written above are the publication
-    consumer_sync();  // every thread is done reading the warp states in comb
-    if (!merge_splits(p, p.partials + (size_t)it * kGroup * kPartialStride, ns, O0, M0, L0, comb,
+    consumer_sync();  // comb is free again; split 0's own partials are written
+    if (!merge_splits(p, p.partials + (size_t)it * kGroup * kPartialStride, ns, comb,
                       p.part_tag0 + (uint32_t)layer,
                       p.attn + (size_t)a.b * p.NQ * kHeadDim + a.g * kGroup * kHeadDim,
                       phase_tag(p, layer * 5 + 1), 3100 + layer))
