@@ -252,8 +252,11 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
  * fp32 accumulation, Y bf16 (out) or fp32 (out_f32, no residual). W is a
  * weight matrix in HF [out][in] layout (any n, k a multiple of 64); X has
  * rows_padded (16, 32 or 64) rows of which the first `rows` are real and the
- * rest zero. Narrow W is split along k across CTAs; then `workspace` must
- * hold mk_gemm_workspace(n, k, rows) bytes. *error (device) is set to
+ * rest zero. Narrow W is split along k over the CTAs of a thread-block
+ * cluster whose partial sums meet in distributed shared memory, so no
+ * workspace is needed: mk_gemm_workspace returns 0 and `workspace` may be
+ * NULL (both stay in the interface for callers written against a split-K
+ * workspace). *error (device) is set to
  * 101-103 when one of the kernel's (time-bounded) waits ran out. Asynchronous. These
  * are the projections of the reference's decoder (attention.py:95-245,
  * :409-448, mlp.py:60-192, the lm_head llama.py:1208-1227) at batch > 1. */

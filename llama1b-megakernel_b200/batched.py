@@ -63,7 +63,7 @@ class BatchedDecoder:
         gws = max(self.lib.mk_gemm_workspace(n, k, max_batch) for n, k in (
             ((c.num_q_heads + 2 * c.num_kv_heads) * 64, c.hidden), (c.hidden, c.num_q_heads * 64),
             (2 * c.intermediate, c.hidden), (c.hidden, c.intermediate), (c.vocab, c.hidden)))
-        self.gwork = torch.zeros(max(gws, 16), dtype=torch.uint8, device=self.dev)  # counters start at 0
+        self.gwork = torch.zeros(max(gws, 16), dtype=torch.uint8, device=self.dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self._graphs: dict[int, tuple] = {}
 
@@ -190,7 +190,6 @@ class BatchedDecoder:
         code = int(self.err[0])
         if code:
             self.err.zero_()
-            self.gwork.zero_()  # a failed split-K GEMM can leave its tile counters mid-count
             what = ("a block table names a page outside the pool" if code == 1 else
                     f"a tcgen05 GEMM wait ran out (code {code})")
             raise _lib.MkError(_lib.MK_EDEVICE, f"batched step: {what}")

@@ -412,9 +412,11 @@ int encode_sw128(CUtensorMap* out, const void* base, long long rows, long long c
 
 // K blocks per split for an n x k GEMM: narrow W is split along K so the
 // grid covers the SMs.
+constexpr int kGemmMaxCluster = 8;  // portable thread-block cluster size
 int gemm_kblocks_per_split(int n, int k, int sms) {
   const int tiles = (n + mk::kGemmTileN - 1) / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
   int splits = tiles >= sms / 2 ? 1 : (sms + tiles - 1) / tiles;
+  if (splits > kGemmMaxCluster) splits = kGemmMaxCluster;  // one cluster per tile
   if (splits > kblocks) splits = kblocks;
   return (kblocks + splits - 1) / splits;
 }
@@ -428,8 +430,24 @@ cudaError_t launch_gemm(const mk::GemmParams& gp, int tiles, int splits, cudaStr
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  mk::gemm_kernel<BP><<<dim3(tiles, splits), mk::kGemmThreads, smem, st>>>(gp);
-  return cudaGetLastError();
+  if (splits == 1) {
+    mk::gemm_kernel<BP><<<dim3(tiles, 1), mk::kGemmThreads, smem, st>>>(gp);
+    return cudaGetLastError();
+  }
+  // the K splits of a tile form one cluster (their sums meet in shared memory)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, splits);
+  cfg.blockDim = dim3(mk::kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr_c[1];
+  attr_c[0].id = cudaLaunchAttributeClusterDimension;
+  attr_c[0].val.clusterDim.x = 1;
+  attr_c[0].val.clusterDim.y = splits;
+  attr_c[0].val.clusterDim.z = 1;
+  cfg.attrs = attr_c;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mk::gemm_kernel<BP>, gp);
 }
 }  // namespace
 
@@ -855,12 +873,10 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
 }
 
 int64_t mk_gemm_workspace(int32_t n, int32_t k, int32_t rows) {
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (n < 1 || k < mk::kGemmTileK || rows < 1) return 0;
-  const int kps = gemm_kblocks_per_split(n, k, sms);
-  const int splits = (k / mk::kGemmTileK + kps - 1) / kps;
-  return splits > 1 ? (int64_t)splits * rows * n * 4 : 0;
+  (void)n;
+  (void)k;
+  (void)rows;
+  return 0;  // split-K sums meet in distributed shared memory, not in a workspace
 }
 
 int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t rows,
@@ -881,8 +897,8 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
   const int tiles = (n + mk::kGemmTileN - 1) / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
   const int kps = gemm_kblocks_per_split(n, k, sms);
   const int splits = (kblocks + kps - 1) / kps;
-  if (splits > 1 && (!workspace || workspace_bytes < (int64_t)splits * rows * n * 4))
-    return fail(MK_EINVAL, "split-K needs a workspace of %lld bytes", (long long)splits * rows * n * 4);
+  (void)workspace;
+  (void)workspace_bytes;
   mk::GemmParams gp{};
   if (int rc = encode_sw128(&gp.tm_w, w, n, k, mk::kGemmTileN)) return rc;
   if (int rc = encode_sw128(&gp.tm_x, x, rows_padded, k, rows_padded)) return rc;
@@ -890,10 +906,10 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
   gp.K = k;
   gp.B = rows;
   gp.kblocks_per_split = kps;
-  gp.residual = splits > 1 ? nullptr : static_cast<const mk::bf16*>(residual);
-  gp.out = splits > 1 ? nullptr : static_cast<mk::bf16*>(out);
-  gp.out_f32 = splits > 1 ? nullptr : out_f32;
-  gp.partial = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  gp.splits = splits;
+  gp.residual = static_cast<const mk::bf16*>(residual);
+  gp.out = static_cast<mk::bf16*>(out);
+  gp.out_f32 = out_f32;
   gp.error = error;
   gp.timeout_ns = 2000000000ull;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -901,13 +917,6 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
                   : rows_padded == 32 ? launch_gemm<32>(gp, tiles, splits, st)
                                       : launch_gemm<64>(gp, tiles, splits, st);
   if (e != cudaSuccess) return fail(MK_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
-  if (splits > 1) {
-    const int bn = rows * n;
-    mk::gemm_reduce_kernel<<<(bn + 255) / 256, 256, 0, st>>>(
-        static_cast<const float*>(workspace), splits, bn, static_cast<const mk::bf16*>(residual),
-        static_cast<mk::bf16*>(out), out_f32);
-    MK_CUDA(cudaGetLastError());
-  }
   return MK_OK;
 }
 

@@ -15,9 +15,12 @@
 //    epilogue;
 //  * four warps read the accumulator back (tcgen05.ld.32x32b: warp w owns
 //    TMEM lanes = W rows 32w..32w+31) and write Y[b][n] (coalesced along n);
-//  * narrow W (16-24 tiles for 148 SMs) is split along K: each split writes
-//    fp32 partial sums and a second kernel adds them in split order, adds the
-//    residual and rounds once to bf16.
+//  * narrow W (16-24 tiles for 148 SMs) is split along K over the CTAs of a
+//    thread-block cluster (at most 8, one cluster per tile): each CTA stages
+//    its fp32 accumulator in its (then idle) ring memory, and after a cluster
+//    barrier rank r adds slice r of the tile over all ranks' stages through
+//    distributed shared memory, in split order, adds the residual and rounds
+//    once to bf16 — no partial sums in global memory, no second kernel.
 // Every mbarrier wait is time-bounded (flag + early exit), and a CTA waits for
 // its own in-flight copies and MMAs before it releases shared memory and TMEM.
 #pragma once
@@ -38,10 +41,10 @@ struct GemmParams {
   CUtensorMap tm_x;  // X [BP][K] bf16: dims {K, BP}, box {64, BP}, 128B swizzle
   int N, K, B;       // B: real rows of X (<= BP)
   int kblocks_per_split;
+  int splits;                     // CTAs along K = the cluster size (1: no split)
   const __nv_bfloat16* residual;  // [B][N] or null
   __nv_bfloat16* out;             // [B][N] bf16 (no split)
-  float* out_f32;                 // [B][N] fp32 (no split; e.g. logits)
-  float* partial;                 // [splits][B][N] fp32 (split-K)
+  float* out_f32;                 // [B][N] fp32 (e.g. logits)
   int* error;
   unsigned long long timeout_ns;
 };
@@ -135,6 +138,16 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[BP]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < BP; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One output element: fp32 as is, or + residual and one bf16 rounding.
+__device__ __forceinline__ void g_store(const GemmParams& p, size_t o, float y) {
+  if (p.out_f32) {
+    p.out_f32[o] = y;
+    return;
+  }
+  if (p.residual) y += __bfloat162float(p.residual[o]);
+  p.out[o] = __float2bfloat16_rn(y);
 }
 
 template <int BP>
@@ -236,22 +249,46 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   float v[BP];
   tmem_ld_cols<BP>(tmem + ((uint32_t)(warp * 32) << 16), v);
-  const int n = tile * kGemmTileN + warp * 32 + lane;
-  if (good && n < p.N) {  // rows past N (the last tile's) were zero-filled by TMA
+  if (p.splits == 1) {
+    const int n = tile * kGemmTileN + warp * 32 + lane;
+    if (good && n < p.N) {  // rows past N (the last tile's) were zero-filled by TMA
 #pragma unroll
-    for (int b = 0; b < BP; ++b) {
-      if (b >= p.B) break;
-      const size_t o = (size_t)b * p.N + n;
-      if (p.partial) {
-        p.partial[(size_t)split * p.B * p.N + o] = v[b];
-      } else if (p.out_f32) {
-        p.out_f32[o] = v[b];
-      } else {
-        float y = v[b];
-        if (p.residual) y += __bfloat162float(p.residual[o]);
-        p.out[o] = __float2bfloat16_rn(y);
+      for (int b = 0; b < BP; ++b) {
+        if (b >= p.B) break;
+        g_store(p, (size_t)b * p.N + n, v[b]);
       }
     }
+  } else {
+    // Stage the accumulator as [b][row] (consecutive threads, consecutive
+    // words), then rank `split` sums its slice of the B x 128 outputs over
+    // the cluster's stages in split order. Both cluster barriers are reached
+    // by every thread on every path, so no CTA waits for one that left.
+    const int r = warp * 32 + lane;
+#pragma unroll
+    for (int b = 0; b < BP; ++b)
+      asm volatile("st.shared.f32 [%0], %1;" ::"r"(ring + (uint32_t)(b * kGemmTileN + r) * 4),
+                   "f"(good ? v[b] : 0.f)
+                   : "memory");
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+    const int E = p.B * kGemmTileN;
+    const int e1 = (split + 1) * E / p.splits;
+    for (int i = split * E / p.splits + threadIdx.x; i < e1; i += kGemmThreads) {
+      const uint32_t local = ring + (uint32_t)i * 4;
+      float y = 0.f;
+      for (int q = 0; q < p.splits; ++q) {
+        uint32_t remote;
+        float t;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(q));
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(t) : "r"(remote) : "memory");
+        y += t;
+      }
+      const int n = tile * kGemmTileN + (i % kGemmTileN);
+      if (good && n < p.N) g_store(p, (size_t)(i / kGemmTileN) * p.N + n, y);
+    }
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -268,22 +305,6 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
                  "r"((uint32_t)(BP < 32 ? 32 : BP))
                  : "memory");
   }
-}
-
-// Split-K reduction: out[b][n] = bf16(sum_s partial[s][b][n] + residual[b][n]).
-__global__ void __launch_bounds__(256) gemm_reduce_kernel(const float* partial, int splits, int BN,
-                                                          const __nv_bfloat16* residual,
-                                                          __nv_bfloat16* out, float* out_f32) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= BN) return;
-  float y = 0.f;
-  for (int s = 0; s < splits; ++s) y += partial[(size_t)s * BN + i];
-  if (out_f32) {
-    out_f32[i] = y;
-    return;
-  }
-  if (residual) y += __bfloat162float(residual[i]);
-  out[i] = __float2bfloat16_rn(y);
 }
 
 }  // namespace mk
