@@ -412,6 +412,24 @@ int encode_sw128(CUtensorMap* out, const void* base, long long rows, long long c
 
 // K blocks per split for an n x k GEMM: narrow W is split along K so the
 // grid covers the SMs.
+// Launch with programmatic stream serialization: the kernel (which calls
+// pdl_trigger / pdl_wait) may start while the previous one in the stream ends.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 constexpr int kGemmMaxCluster = 8;  // portable thread-block cluster size
 int gemm_kblocks_per_split(int n, int k, int sms) {
   const int tiles = (n + mk::kGemmTileN - 1) / mk::kGemmTileN, kblocks = k / mk::kGemmTileK;
@@ -430,23 +448,22 @@ cudaError_t launch_gemm(const mk::GemmParams& gp, int tiles, int splits, cudaStr
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  if (splits == 1) {
-    mk::gemm_kernel<BP><<<dim3(tiles, 1), mk::kGemmThreads, smem, st>>>(gp);
-    return cudaGetLastError();
-  }
+  if (splits == 1) return launch_pdl(mk::gemm_kernel<BP>, dim3(tiles, 1), dim3(mk::kGemmThreads), smem, st, gp);
   // the K splits of a tile form one cluster (their sums meet in shared memory)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, splits);
   cfg.blockDim = dim3(mk::kGemmThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr_c[1];
+  cudaLaunchAttribute attr_c[2];
   attr_c[0].id = cudaLaunchAttributeClusterDimension;
   attr_c[0].val.clusterDim.x = 1;
   attr_c[0].val.clusterDim.y = splits;
   attr_c[0].val.clusterDim.z = 1;
+  attr_c[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr_c[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr_c;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, mk::gemm_kernel<BP>, gp);
 }
 }  // namespace
@@ -865,10 +882,9 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
                                  mk::kAttnSmem));
     attr = true;
   }
-  mk::paged_attn_kernel<<<dim3(ap.splits, num_kv_heads, batch), mk::kAttnCtaWarps * 32, mk::kAttnSmem, st>>>(ap);
-  MK_CUDA(cudaGetLastError());
-  mk::paged_attn_merge_kernel<<<dim3(num_kv_heads, batch), 256, 0, st>>>(ap);
-  MK_CUDA(cudaGetLastError());
+  MK_CUDA(launch_pdl(mk::paged_attn_kernel, dim3(ap.splits, num_kv_heads, batch),
+                     dim3(mk::kAttnCtaWarps * 32), mk::kAttnSmem, st, ap));
+  MK_CUDA(launch_pdl(mk::paged_attn_merge_kernel, dim3(num_kv_heads, batch), dim3(256), 0, st, ap));
   return MK_OK;
 }
 
@@ -925,10 +941,10 @@ int mk_rmsnorm_rows(const void* x, const void* gamma, float eps, int32_t rows, i
   if (!x || !gamma || !out) return fail(MK_EINVAL, "NULL argument");
   if (rows < 1 || hidden < 8 || hidden % 8) return fail(MK_EINVAL, "rows %d, hidden %d", rows, hidden);
   if (!aligned16(x) || !aligned16(gamma) || !aligned16(out)) return fail(MK_EINVAL, "16-byte alignment");
-  mk::rmsnorm_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const mk::bf16*>(x), static_cast<const mk::bf16*>(gamma), eps, hidden,
-      static_cast<mk::bf16*>(out));
-  MK_CUDA(cudaGetLastError());
+  MK_CUDA(launch_pdl(mk::rmsnorm_rows_kernel, dim3(rows), dim3(256), 0,
+                     static_cast<cudaStream_t>(stream), static_cast<const mk::bf16*>(x),
+                     static_cast<const mk::bf16*>(gamma), eps, (int)hidden,
+                     static_cast<mk::bf16*>(out)));
   return MK_OK;
 }
 
@@ -943,20 +959,20 @@ int mk_rope_scatter(const void* qkv, const void* rope_cos, const void* rope_sin,
   if (batch < 1 || num_q_heads < 1 || num_kv_heads < 1 || page_size < 1 || max_blocks < 1)
     return fail(MK_EINVAL, "geometry");
   const int n = batch * (num_q_heads + 2 * num_kv_heads) * 32;
-  mk::rope_scatter_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const mk::bf16*>(qkv), static_cast<const mk::bf16*>(rope_cos),
-      static_cast<const mk::bf16*>(rope_sin), positions, block_tables, max_blocks, num_pages,
-      page_size, num_q_heads, num_kv_heads, batch, static_cast<mk::bf16*>(q_out),
-      static_cast<mk::bf16*>(k_pages), static_cast<mk::bf16*>(v_pages), error);
-  MK_CUDA(cudaGetLastError());
+  MK_CUDA(launch_pdl(mk::rope_scatter_kernel, dim3((n + 255) / 256), dim3(256), 0,
+                     static_cast<cudaStream_t>(stream), static_cast<const mk::bf16*>(qkv),
+                     static_cast<const mk::bf16*>(rope_cos), static_cast<const mk::bf16*>(rope_sin),
+                     positions, block_tables, (int)max_blocks, (int)num_pages, (int)page_size,
+                     (int)num_q_heads, (int)num_kv_heads, (int)batch, static_cast<mk::bf16*>(q_out),
+                     static_cast<mk::bf16*>(k_pages), static_cast<mk::bf16*>(v_pages), error));
   return MK_OK;
 }
 
 int mk_swiglu(const void* gate_up, int64_t n, void* out, void* stream) {
   if (!gate_up || !out || n < 1 || n > INT32_MAX) return fail(MK_EINVAL, "arguments");
-  mk::swiglu_kernel<<<(int)((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const mk::bf16*>(gate_up), (int)n, static_cast<mk::bf16*>(out));
-  MK_CUDA(cudaGetLastError());
+  MK_CUDA(launch_pdl(mk::swiglu_kernel, dim3((int)((n + 255) / 256)), dim3(256), 0,
+                     static_cast<cudaStream_t>(stream), static_cast<const mk::bf16*>(gate_up), (int)n,
+                     static_cast<mk::bf16*>(out)));
   return MK_OK;
 }
 

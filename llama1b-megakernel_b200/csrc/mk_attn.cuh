@@ -30,6 +30,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "mk_device.cuh"
+
 namespace mk {
 
 constexpr int kAttnCtaWarps = 4;
@@ -64,6 +66,8 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32
 __device__ __forceinline__ uint32_t swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
 __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __grid_constant__ PagedAttnParams p) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t asmem[];
   __shared__ float st[kAttnCtaWarps][4][kAttnPartial];     // per-warp states
   const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
@@ -258,6 +262,8 @@ __global__ void __launch_bounds__(kAttnCtaWarps * 32) paged_attn_kernel(const __
 }
 
 __global__ void __launch_bounds__(256) paged_attn_merge_kernel(const __grid_constant__ PagedAttnParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int g = blockIdx.x, b = blockIdx.y;
   const int h = threadIdx.x >> 6, d = threadIdx.x & 63;
   const float* src = p.work + (((size_t)b * p.NKV + g) * p.splits * 4) * kAttnPartial;

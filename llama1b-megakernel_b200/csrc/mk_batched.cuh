@@ -14,6 +14,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "mk_device.cuh"
+
 namespace mk {
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -21,6 +23,8 @@ __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2
 // One CTA of 256 threads per row; H a multiple of 8.
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const __nv_bfloat16* x, const __nv_bfloat16* gamma,
                                                            float eps, int H, __nv_bfloat16* y) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[8];
   const int b = blockIdx.x, tid = threadIdx.x;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)b * H);
@@ -67,6 +71,8 @@ __global__ void __launch_bounds__(256) rope_scatter_kernel(
     const __nv_bfloat16* qkv, const __nv_bfloat16* cos_t, const __nv_bfloat16* sin_t,
     const int* positions, const int* block_tables, int max_blocks, int num_pages, int ps, int NQ,
     int NKV, int B, __nv_bfloat16* q_out, __nv_bfloat16* k_pages, __nv_bfloat16* v_pages, int* error) {
+  pdl_trigger();
+  pdl_wait();
   const int nh = NQ + 2 * NKV;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= B * nh * 32) return;
@@ -104,6 +110,8 @@ __global__ void __launch_bounds__(256) rope_scatter_kernel(
 
 // gu: [B][I][2] (gate, up interleaved, the packed w_gate_up order) -> a [B][I].
 __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* gu, int n, __nv_bfloat16* a) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const __nv_bfloat162 p = reinterpret_cast<const __nv_bfloat162*>(gu)[i];

@@ -58,6 +58,15 @@ enum Counter : int {
   kCounters = 4,  // words in the counter block
 };
 
+// Programmatic dependent launch (the batched path's kernels, launched with
+// the programmatic-serialization attribute): pdl_trigger lets the next kernel
+// of the stream start its prologue; pdl_wait blocks until the kernels this one
+// depends on have finished and their writes are visible (without the
+// attribute both are no-ops). A kernel touches no global memory before
+// pdl_wait.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -29,6 +29,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "mk_device.cuh"
+
 namespace mk {
 
 constexpr int kGemmStages = 4;  // 96 KB: two CTAs per SM overlap one tile's epilogue with the next's loads
@@ -167,6 +169,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   const int kb1 = min(p.K / kGemmTileK, kb0 + p.kblocks_per_split);
   const int nk = kb1 - kb0;
   auto sa = [](uint64_t* b) { return (uint32_t)__cvta_generic_to_shared(b); };
+  pdl_trigger();  // barrier init and TMEM allocation below overlap the previous kernel
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemmStages; ++s) {
@@ -187,6 +190,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
+  pdl_wait();  // X (and the residual) come from the previous kernel
 
   if (warp == 0 && lane == 0) {
     // ---- producer: TMA boxes of W rows [tile*128, +128) and all X rows
