@@ -285,6 +285,13 @@ int mk_rope_scatter(const void* qkv, const void* rope_cos, const void* rope_sin,
                     void* v_pages, int32_t* error, void* stream);
 int mk_swiglu(const void* gate_up, int64_t n, void* out, void* stream);
 
+/* Greedy ids of `rows` rows of fp32 logits [rows][cols] (128-bit loads when
+ * cols is a multiple of 4 and x 16-byte aligned): ids[r] = the first column
+ * holding the row's maximum, as
+ * the reference's greedy sampling takes the argmax of the logits
+ * (llama.py:1208-1227, torch.argmax). Asynchronous. */
+int mk_argmax_rows(const float* x, int32_t rows, int32_t cols, int64_t* ids, void* stream);
+
 /* ---- Tensor parallelism (one decode step over `world` GPUs) --------------
  *
  * Each rank's handle is made with mk_init from the rank's LOCAL geometry:

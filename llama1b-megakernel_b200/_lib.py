@@ -25,7 +25,7 @@ EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_schedule_gap", "mk_sample", "mk_paged_attention_workspace",
-    "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
+    "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_argmax_rows", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
     "mk_destroy",
 )
 
@@ -109,6 +109,7 @@ def load() -> ctypes.CDLL:
     lib.mk_rope_scatter.argtypes = [VP, VP, VP, VP, VP, I32, I32, I32, I32, I32, I32, VP, VP, VP,
                                     VP, VP]
     lib.mk_swiglu.argtypes = [VP, ctypes.c_int64, VP, VP]
+    lib.mk_argmax_rows.argtypes = [VP, I32, I32, VP, VP]
     lib.mk_tp_setup.argtypes = [VP, I32, I32, I32, I32, P(MkIpcHandle), P(VP)]
     lib.mk_tp_connect.argtypes = [VP, P(MkIpcHandle), P(VP)]
     lib.mk_last_error.argtypes = []

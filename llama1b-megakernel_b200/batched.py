@@ -126,7 +126,7 @@ class BatchedDecoder:
         _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_final.data_ptr(), eps, B, H,
                                        h.data_ptr(), st))
         self._gemm(pw.embed, h, B, out_f32=logits_out)
-        ids_out.copy_(logits_out.argmax(dim=-1))
+        _lib.check(lib.mk_argmax_rows(logits_out.data_ptr(), B, c.vocab, ids_out.data_ptr(), st))
 
     def _graph(self, B: int):
         g = self._graphs.get(B)

@@ -968,6 +968,15 @@ int mk_rope_scatter(const void* qkv, const void* rope_cos, const void* rope_sin,
   return MK_OK;
 }
 
+int mk_argmax_rows(const float* x, int32_t rows, int32_t cols, int64_t* ids, void* stream) {
+  if (!x || !ids || rows < 1 || cols < 1)
+    return fail(MK_EINVAL, "argmax: x, ids, rows >= 1 and cols >= 1 are required");
+  const bool vec = cols % 4 == 0 && aligned16(x);
+  MK_CUDA(launch_pdl(mk::argmax_rows_kernel, dim3(rows), dim3(1024), 0,
+                     static_cast<cudaStream_t>(stream), x, (int)cols, vec, ids));
+  return MK_OK;
+}
+
 int mk_swiglu(const void* gate_up, int64_t n, void* out, void* stream) {
   if (!gate_up || !out || n < 1 || n > INT32_MAX) return fail(MK_EINVAL, "arguments");
   MK_CUDA(launch_pdl(mk::swiglu_kernel, dim3((int)((n + 255) / 256)), dim3(256), 0,

@@ -9,6 +9,7 @@
 //             for the pair (d, d + 32) of every q and k head, from the bf16
 //             cos/sin table rows of the step's positions
 //   swiglu:   a = bf16(bf16(g / (1 + exp(-g))) * u)
+//   argmax:   the greedy id of each row of fp32 logits (lowest index on ties)
 #pragma once
 
 #include <cuda_bf16.h>
@@ -118,6 +119,70 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* gu, in
   const float g = __bfloat162float(p.x), u = __bfloat162float(p.y);
   const float s = bfr(__fdiv_rn(g, 1.0f + expf(-g)));
   a[i] = __float2bfloat16_rn(s * u);
+}
+
+// One CTA of 1024 threads per row of `cols` fp32 values: each thread scans
+// columns in order (128-bit loads when cols is a multiple of 4 and x 16-byte
+// aligned) and keeps its first maximum; the CTA keeps the largest value, then
+// the lowest index.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* x, int cols, bool vec,
+                                                           int64_t* ids) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const float* rowf = x + (size_t)blockIdx.x * cols;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  if (vec) {
+    const float4* row = reinterpret_cast<const float4*>(rowf);
+    for (int i = threadIdx.x; i < cols / 4; i += 1024) {
+      const float4 v = __ldg(row + i);
+      const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (e[k] > best) {
+          best = e[k];
+          idx = 4 * i + k;
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < cols; i += 1024) {
+      const float v = __ldg(rowf + i);
+      if (v > best) {
+        best = v;
+        idx = i;
+      }
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = idx;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = bv[lane];
+    idx = bi[lane];
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > best || (ov == best && oi < idx)) {
+        best = ov;
+        idx = oi;
+      }
+    }
+    if (lane == 0) ids[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
+  }
 }
 
 }  // namespace mk
