@@ -1,24 +1,34 @@
 """Benchmark: bs=1 Llama-3.2-1B greedy decode on B200 through the megakernel.
 
-Workload: seeded random-init Llama-3.2-1B in bf16, a
-128-token seeded prompt (fed through the decode kernel one position per
-launch, untimed), then greedy decode steps from position 128 on, max context
-1024. One step = one launch of the persistent kernel = all 16 layers + final
-norm + lm_head + argmax for one token; the argmax feeds the next launch on the
-device (no host round trip). ``value`` = tokens/s over the K timed steps
-(CUDA events on the launching stream), max over ranks.
+Headline workload (BASELINE.json's metric, "bs=1 decode tok/s & p50 token
+latency at ctx 1024"): seeded random-init Llama-3.2-1B in bf16, a paged KV
+cache pre-filled with 1024 seeded N(0,1) bf16 positions, a seeded random
+token, then K back-to-back greedy decode steps from position 1024 (the cache
+and RoPE table sized for 1024 + K + warm-up). One step = one launch of the
+persistent kernel = all 16 layers + final norm + lm_head + argmax for one
+token; the argmax feeds the next launch on the device (no host round trip).
+``value`` = tokens/s over the K timed steps (CUDA events on the launching
+stream), max over ranks; ``p50_ms`` / ``p90_ms`` / ``p99_ms`` per step.
 
-``e2e`` runs the same steps through the public API
-(``MegakernelLlamaForCausalLM.forward`` with a pinned host token and
-position, H2D copy, launch, D2H of the next id, host sync per step).
+``e2e`` runs the same steps, from position 1024 on a cache filled the same
+way, through the public API (``MegakernelLlamaForCausalLM.forward`` with a
+pinned host token and position: H2D copy, launch, D2H of the next id, host
+sync per step).
 
 ``roofline``: algorithmic bytes per step (2,471,632,896 B of weights + 32,768 B
-per cached position read + 32,768 B of K/V written) / average step time,
-against the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+per cached position read + 32,768 B of K/V written, at the timed steps' mean
+position) / average step time, against the measured HBM copy bandwidth in
+MEASURED_PEAKS.json.
 
-``--impl reference``: the reference's PyTorch Llama path (HF
-``LlamaForCausalLM``, via oracle/) timed on the host CPU cores on a bounded
-sample of the same workload; rank 0 only.
+Extras: ``decode_640`` (a 128-token seeded prompt, then 640
+greedy steps), ``ctx_sweep`` (config 3: one step at 128 / 1024 / 4096 / 8192
+cached positions), ``batched`` (config 4: bs 8 / 32 / 64 at KV 1024).
+
+``cpu_baseline`` and ``--impl reference``: the reference's PyTorch Llama path
+(HF ``LlamaForCausalLM``, via oracle/) on the host CPU cores on BASELINE
+config 1 exactly: one greedy step at position 1024 over the same 1024 cached
+rows and the same token (the cache is cropped back to 1024 after every step),
+timed over several steps; rank 0 only.
 
 Multi-GPU (torchrun, N > 1): tensor-parallel decode
 of the one sequence over the N GPUs (``TensorParallelLlamaForCausalLM``: q/kv
@@ -45,15 +55,19 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "bs=1 decode tok/s & p50 token latency at ctx 1024; % of 8 TB/s HBM roofline"
-PROMPT_LEN = 128
-MAX_CTX = 1024
+PROMPT_LEN = 128          # config 2's prompt
+DECODE_STEPS = 640       # config 2's greedy steps
+CTX = 1024               # the headline's context: cached positions before the first step
+KV_SEED, TOKEN_SEED = 1024, 9
 FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = ("Llama-3.2-1B bs=1 greedy decode at ctx 1024: 1024 cached N(0,1) bf16 positions "
+            "(seeded), seeded random token, steps from position 1024")
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=640)
+    ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--replicas", action="store_true",
@@ -62,16 +76,17 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the ctx sweep extra")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the bs 8/32/64 extra")
-    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a few steps, no e2e / sweep / cpu baseline")
-    ap.add_argument("--case", choices=["small4", "gemm", "batched"], default=None,
+    ap.add_argument("--case", choices=["small4", "gemm", "batched", "trace"], default=None,
                     help="ncu profiling cases (print timings, no JSON line): small4 - 4 "
                          "Llama-3.2-1B layers, vocab 32000, one step at ctx 512 after 4 warm-up "
                          "steps; gemm - the tcgen05 GEMM on the batched projection shapes at 8 "
                          "and 64 rows (3 warm-up + 7 timed launches each, L2 flushed, cuBLAS "
                          "beside it); batched - one bs-64 batched step at KV 1024 replayed "
-                         "inside the NVTX range 'replay'")
+                         "inside the NVTX range 'replay'; trace - the per-phase trace of "
+                         "Llama-3.2-1B steps at ctx 1024 (mk_set_trace, summarised by trace.py)")
     return ap.parse_args()
 
 
@@ -183,9 +198,25 @@ def traffic_summary():
 # CPU: the reference's PyTorch path (HF Llama) on the host cores
 # ----------------------------------------------------------------------------
 
-def cpu_reference(weights_cpu, seconds: float, ctx: int = 448):
-    """HF LlamaForCausalLM decode steps on CPU at context ~ctx (the workload's
-    mean context: 128 prompt + 640 steps / 2). Returns (tok/s, detail)."""
+def cpu_model_name() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_config1(weights_cpu, seconds: float, min_steps: int = 5, max_steps: int | None = None,
+                warmup: int = 1):
+    """BASELINE config 1 on the host CPU: HF LlamaForCausalLM (the reference's
+    PyTorch Llama path) in bf16, one greedy decode step at position 1024 over
+    1024 cached N(0,1) positions (the GPU arm's cache rows and token). The
+    cache is cropped back to 1024 positions after every step, so every timed
+    step is that same step. Runs ``warmup`` untimed steps, then timed steps
+    until ``seconds`` have passed (at least ``min_steps``, at most
+    ``max_steps``). Returns (tok/s, detail)."""
     from transformers import DynamicCache
 
     from llama1b_megakernel_b200 import synthetic as syn
@@ -195,34 +226,28 @@ def cpu_reference(weights_cpu, seconds: float, ctx: int = 448):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     model = O.hf_model(cfg, weights_cpu)
-    k, v = syn.random_kv_rows(cfg, ctx, seed=7)
+    k, v = syn.random_kv_rows(cfg, CTX, seed=KV_SEED)
     cache = DynamicCache(config=model.config)
     for l in range(cfg.num_layers):
         cache.update(k[l:l + 1].clone(), v[l:l + 1].clone(), l)
-    tok = int(syn.random_tokens(1, cfg.vocab, seed=9)[0])
-    times = []
+    tok = int(syn.random_tokens(1, cfg.vocab, seed=TOKEN_SEED)[0])
+    ids, pos = torch.tensor([[tok]]), torch.tensor([[CTX]])
+    times, nxt = [], None
     with torch.no_grad():
+        for _ in range(warmup):
+            model(input_ids=ids, position_ids=pos, past_key_values=cache, use_cache=True)
+            cache.crop(CTX)
         t_end = time.perf_counter() + seconds
-        pos = ctx
-        while time.perf_counter() < t_end or len(times) < 3:
+        while (time.perf_counter() < t_end or len(times) < min_steps) and \
+                (max_steps is None or len(times) < max_steps):
             t0 = time.perf_counter()
-            out = model(input_ids=torch.tensor([[tok]]), position_ids=torch.tensor([[pos]]),
-                        past_key_values=cache, use_cache=True)
-            tok = int(out.logits[0, -1].argmax())
+            out = model(input_ids=ids, position_ids=pos, past_key_values=cache, use_cache=True)
+            nxt = int(out.logits[0, -1].argmax())
             times.append(time.perf_counter() - t0)
-            pos += 1
-    steps = len(times) - 1  # first step warms the allocator
-    tps = steps / sum(times[1:])
-    cpu = "unknown"
-    try:
-        for ln in Path("/proc/cpuinfo").read_text().splitlines():
-            if ln.startswith("model name"):
-                cpu = ln.split(":", 1)[1].strip()
-                break
-    except OSError:
-        pass
-    return tps, {"cores": threads, "cpu_model": cpu, "steps": steps, "ctx_start": ctx,
-                 "p50_ms": statistics.median(times[1:]) * 1e3}
+            cache.crop(CTX)
+    tps = len(times) / sum(times)
+    return tps, {"cores": threads, "cpu_model": cpu_model_name(), "steps": len(times),
+                 "p50_ms": statistics.median(times) * 1e3, "next_id": nxt}
 
 
 def run_reference(args, ws, rank):
@@ -233,17 +258,19 @@ def run_reference(args, ws, rank):
 
     w = syn.make_weights(cfg, seed=0, device="cuda" if torch.cuda.is_available() else "cpu")
     w = {k: t.cpu() for k, t in w.items()}
-    tps, det = cpu_reference(w, args.cpu_seconds)
-    sample = (f"HF LlamaForCausalLM (reference's PyTorch Llama path) bf16 on CPU, "
-              f"{det['steps']} greedy decode steps from ctx {det['ctx_start']}, "
-              f"{det['cores']} threads, {det['cpu_model']}")
+    K, W = args.steps, args.warmup
+    tps, det = cpu_config1(w, seconds=0.0, min_steps=K, max_steps=K, warmup=W)
+    sample = (f"HF LlamaForCausalLM (the reference's PyTorch Llama path) bf16 on CPU: BASELINE "
+              f"config 1, one greedy step at position {CTX} over {CTX} cached N(0,1) positions, "
+              f"{det['steps']} timed steps after {W} warm-up, {det['cores']} threads, "
+              f"{det['cpu_model']}")
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s",
-        "n_gpus": args.gpus, "steps": det["steps"], "warmup": 1,
+        "n_gpus": args.gpus, "steps": det["steps"], "warmup": W,
         "ms_per_step": 1e3 / tps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights)",
-        "config": {"workload": "Llama-3.2-1B bs=1 greedy decode (sample at ctx ~448)",
-                   "global_batch": 1, "seq_len": MAX_CTX, "parallelism": "cpu"},
+        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": CTX,
+                   "parallelism": "cpu"},
         "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": det["cores"], "kind": "port",
                          "sample": sample},
         "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -256,6 +283,44 @@ def run_reference(args, ws, rank):
 # GPU: the megakernel
 # ----------------------------------------------------------------------------
 
+def _kv_rows_for(model, cfg, n, seed, dev):
+    """N(0,1) rows of the whole model's cache, this rank's kv heads only."""
+    from llama1b_megakernel_b200 import synthetic as syn
+
+    k, v = syn.random_kv_rows(cfg, n, seed=seed, device=dev)
+    nkv = model.cfg.num_kv_heads
+    r = getattr(model, "tp_rank", 0)
+    return k[:, r * nkv:(r + 1) * nkv].contiguous(), v[:, r * nkv:(r + 1) * nkv].contiguous()
+
+
+def _timed_steps(model, kv, tok, pos, nxt, first_tok, first_pos, K, W, ws):
+    """W untimed and K timed greedy steps from (first_tok, first_pos), the
+    argmax fed back on the device. Returns per-step ms and the total ms
+    (max over ranks)."""
+    def reset():
+        tok.fill_(first_tok)
+        pos.fill_(first_pos)
+
+    reset()
+    for _ in range(W):
+        model.launch(tok, pos, kv, None, nxt, feedback=True)
+    model.sync()
+    reset()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    barrier(ws)
+    torch.cuda.synchronize()
+    for i in range(K):
+        starts[i].record()
+        model.launch(tok, pos, kv, None, nxt, feedback=True)
+        ends[i].record()
+    torch.cuda.synchronize()
+    barrier(ws)
+    model.sync()
+    step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    return step_ms, max_over_ranks(starts[0].elapsed_time(ends[-1]), ws)
+
+
 def run_ours(args, ws, rank, local):
     from llama1b_megakernel_b200 import synthetic as syn
     from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
@@ -266,7 +331,9 @@ def run_ours(args, ws, rank, local):
     hbm_peak, peak_kind = peaks()
     tp_world = ws if (ws > 1 and not args.replicas) else 1
     sweep = not (args.no_sweep or args.small) and tp_world == 1
-    max_seq = 8192 + 64 if sweep else MAX_CTX
+    K, W = args.steps, args.warmup
+    head_len = CTX + K + W + 2
+    max_seq = max(8192 + 64 if sweep else 0, head_len, PROMPT_LEN + DECODE_STEPS + 2)
     w = syn.make_weights(cfg, seed=0, device=dev)
     if tp_world > 1:
         from llama1b_megakernel_b200.tp import TensorParallelLlamaForCausalLM
@@ -282,85 +349,79 @@ def run_ours(args, ws, rank, local):
     del w
     torch.cuda.empty_cache()
 
-    prompt = syn.random_tokens(PROMPT_LEN, cfg.vocab, seed=1).reshape(1, -1)
-    kv = model.kv
-    out = model.forward(prompt, past_key_values=kv, return_logits=False)
-
-    # ------------------------------------------------------------ device loop
-    K, W = args.steps, args.warmup
-    if PROMPT_LEN + K > MAX_CTX:
-        raise SystemExit(f"--steps must keep the context within {MAX_CTX}")
-    kv.reserve(0, MAX_CTX)
     tok = torch.empty(1, dtype=torch.int32, device=dev)
     pos = torch.empty(1, dtype=torch.int32, device=dev)
     nxt = torch.empty(1, dtype=torch.int32, device=dev)
-    first_tok = out.next_ids.to(torch.int32)
+    first_tok = int(syn.random_tokens(1, cfg.vocab, seed=TOKEN_SEED)[0])
 
-    def reset():
-        tok.copy_(first_tok)
-        pos.fill_(PROMPT_LEN)
-
-    reset()
-    for _ in range(W):
-        model.launch(tok, pos, kv, None, nxt, feedback=True)
-    model.sync()
-    reset()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    # ------------------------------------------------------------ headline: ctx 1024
+    kv = model.kv
+    k, v = _kv_rows_for(model, cfg, CTX, KV_SEED, dev)
+    kv.fill(0, k, v)
+    kv.reserve(0, head_len)
+    del k, v
     clocks = ClockSampler(local)
-    barrier(ws)
     clocks.start()
-    torch.cuda.synchronize()
-    for i in range(K):
-        starts[i].record()
-        model.launch(tok, pos, kv, None, nxt, feedback=True)
-        ends[i].record()
-    torch.cuda.synchronize()
-    barrier(ws)
+    step_ms, total_ms = _timed_steps(model, kv, tok, pos, nxt, first_tok, CTX, K, W, ws)
     clk = clocks.stop()
-    model.sync()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = starts[0].elapsed_time(ends[-1])
-    total_ms = max_over_ranks(total_ms, ws)
     seqs = ws // tp_world  # sequences decoded by the whole job
     value = K * seqs / (total_ms / 1e3)
+    srt = sorted(step_ms)
     p50 = statistics.median(step_ms)
-    p90 = sorted(step_ms)[int(0.9 * (K - 1))]
-    p99 = sorted(step_ms)[int(0.99 * (K - 1))]
+    p90 = srt[int(0.9 * (K - 1))]
+    p99 = srt[int(0.99 * (K - 1))]
     kernel_ms = statistics.mean(step_ms)
-    ctx_mean = PROMPT_LEN + (K - 1) / 2.0
+    ctx_mean = CTX + (K - 1) / 2.0
     # per GPU: a tensor-parallel rank streams 1/tp_world of the weights and KV
     bytes_step = (cfg.weight_bytes_per_token() + cfg.kv_bytes_per_position() * ctx_mean +
                   cfg.kv_bytes_per_position()) / tp_world
     achieved = bytes_step / (kernel_ms / 1e3) / 1e9
 
-    # ------------------------------------------------------------ e2e (public API)
+    # ------------------------------------------------------------ e2e (public API), ctx 1024
     e2e_val = None
     h2d = d2h = 0
     if not args.small:
-        n = min(args.e2e_steps, MAX_CTX - PROMPT_LEN)
+        n = K
         kv2 = model.new_cache(max_seq_len=max_seq)
-        model.forward(prompt, past_key_values=kv2, return_logits=False)
+        k, v = _kv_rows_for(model, cfg, CTX, KV_SEED, dev)
+        kv2.fill(0, k, v)
+        kv2.reserve(0, CTX + n + 4)
+        del k, v
         ids = torch.empty(1, 1, dtype=torch.int32).pin_memory()
         ps = torch.empty(1, 1, dtype=torch.int32).pin_memory()
-        ids[0, 0] = int(first_tok[0])
-        kv2.reserve(0, PROMPT_LEN + n + 1)
         for i in range(3):  # warm-up on the same cache positions
-            ps[0, 0] = PROMPT_LEN + i
+            ids[0, 0] = first_tok
+            ps[0, 0] = CTX + i
             model.forward(ids, ps, past_key_values=kv2, return_logits=False)
-        ids[0, 0] = int(first_tok[0])
+        ids[0, 0] = first_tok
         barrier(ws)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for i in range(n):
-            ps[0, 0] = PROMPT_LEN + i
+            ps[0, 0] = CTX + i
             o = model.forward(ids, ps, past_key_values=kv2, return_logits=False)
             ids[0, 0] = int(o.next_ids[0])  # D2H of the result, host feeds it back
         t1 = time.perf_counter()
-        e2e_s = max_over_ranks(t1 - t0, ws)
-        e2e_val = n * seqs / e2e_s
+        e2e_val = n * seqs / max_over_ranks(t1 - t0, ws)
         h2d = 2 * 4   # token id + position (int32) per step
         d2h = 4       # next id (int32) per step
+        del kv2
+
+    # ------------------------------------------------------------ config 2: prompt + 640 steps
+    dec640 = None
+    if not args.small:
+        kv4 = model.new_cache(max_seq_len=max_seq)
+        prompt = syn.random_tokens(PROMPT_LEN, cfg.vocab, seed=1).reshape(1, -1)
+        out = model.forward(prompt, past_key_values=kv4, return_logits=False)
+        kv4.reserve(0, PROMPT_LEN + DECODE_STEPS + 1)
+        ms640, tot640 = _timed_steps(model, kv4, tok, pos, nxt, int(out.next_ids[0]), PROMPT_LEN,
+                                     DECODE_STEPS, 3, ws)
+        dec640 = {"workload": f"{PROMPT_LEN}-token seeded prompt (decode kernel per position), "
+                              f"then {DECODE_STEPS} greedy steps from position {PROMPT_LEN}",
+                  "tok_s": DECODE_STEPS * seqs / (tot640 / 1e3),
+                  "ms_p50": statistics.median(ms640),
+                  "ms_p99": sorted(ms640)[int(0.99 * (DECODE_STEPS - 1))]}
+        del kv4
 
     # ------------------------------------------------------------ ctx sweep
     sweep_res = None
@@ -398,27 +459,28 @@ def run_ours(args, ws, rank, local):
     if sweep and not args.no_batched:
         batched_res = run_batched(model, cfg, dev, hbm_peak)
 
-    # ------------------------------------------------------------ cpu baseline
+    # ------------------------------------------------------------ cpu baseline (config 1)
     cpu_b = None
     if w_cpu is not None:
         del model
         torch.cuda.empty_cache()
-        tps, det = cpu_reference(w_cpu, args.cpu_seconds)
+        tps, det = cpu_config1(w_cpu, args.cpu_seconds)
         cpu_b = {"value": tps, "unit": "tok/s", "cores": det["cores"], "kind": "port",
+                 "p50_ms": det["p50_ms"],
                  "sample": (f"HF LlamaForCausalLM (the reference's PyTorch Llama path, via "
-                            f"oracle/) bf16, {det['steps']} decode steps from ctx "
-                            f"{det['ctx_start']} on {det['cpu_model']}")}
+                            f"oracle/) bf16, BASELINE config 1: one greedy step at position "
+                            f"{CTX} over the same {CTX} cached rows and token, {det['steps']} "
+                            f"timed steps, on {det['cpu_model']}")}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K,
             "warmup": W, "ms_per_step": total_ms / K, "higher_is_better": True,
             "scaling": "strong" if tp_world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random-init weights, seeded random prompt)",
-            "config": {"workload": "Llama-3.2-1B bs=1 greedy decode: 128-token prompt, then "
-                                   f"{K} steps from position 128 (max ctx 1024)",
-                       "global_batch": seqs, "seq_len": MAX_CTX,
+            "data": "synthetic (seeded random-init weights, seeded N(0,1) KV cache and token)",
+            "config": {"workload": WORKLOAD, "global_batch": seqs, "seq_len": CTX,
                        "parallelism": f"tp{tp_world}" if tp_world > 1 else f"replicas x{ws}",
+                       "first_position": CTX, "last_position": CTX + K - 1,
                        "l2": "inputs larger than L2 (2.47 GB of weights streamed per step)"},
             "p50_ms": p50, "p90_ms": p90, "p99_ms": p99,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak,
@@ -432,6 +494,8 @@ def run_ours(args, ws, rank, local):
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
         }
+        if dec640 is not None:
+            line["decode_640"] = dec640
         if sweep_res is not None:
             line["ctx_sweep"] = sweep_res
         if batched_res is not None:
@@ -577,8 +641,60 @@ def run_case_small4():
     print(f"small4 step {ev[0].elapsed_time(ev[1]):.4f} ms")
 
 
+def run_case_trace():
+    """Per-phase trace of the headline workload: Llama-3.2-1B, 1024 cached
+    N(0,1) positions, steps from position 1024; prints the phase table and
+    the attention breakdown of the median of 5 traced steps (by total)."""
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200 import trace as tr
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+    from llama1b_megakernel_b200.model import MegakernelLlamaForCausalLM
+
+    dev = torch.device("cuda", 0)
+    w = syn.make_weights(cfg, seed=0, device=dev)
+    m = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=CTX + 64, page_size=64,
+                                   device=dev)
+    del w
+    k, v = syn.random_kv_rows(cfg, CTX, seed=KV_SEED, device=dev)
+    m.kv.fill(0, k, v)
+    m.kv.reserve(0, CTX + 16)
+    del k, v
+    tok = torch.tensor([int(syn.random_tokens(1, cfg.vocab, seed=TOKEN_SEED)[0])],
+                       dtype=torch.int32, device=dev)
+    pos = torch.tensor([CTX], dtype=torch.int32, device=dev)
+    nxt = torch.empty(1, dtype=torch.int32, device=dev)
+    for _ in range(4):
+        m.launch(tok, pos, m.kv, None, nxt)
+    m.sync()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    ev[0].record()
+    for j in range(5):
+        m.launch(tok, pos, m.kv, None, nxt)
+        ev[j + 1].record()
+    torch.cuda.synchronize()
+    m.sync()
+    plain = [ev[j].elapsed_time(ev[j + 1]) for j in range(5)]
+    buf = m.set_trace(True)
+    runs = []
+    for _ in range(5):
+        m.launch(tok, pos, m.kv, None, nxt)
+        m.sync()
+        runs.append(tr.phase_table(buf.cpu().numpy(), cfg.num_layers))
+        runs[-1]["_attn"] = tr.attention_breakdown(buf.cpu().numpy(), cfg.num_layers)
+    m.set_trace(False)
+    runs.sort(key=lambda r: r["total_us"])
+    med = runs[len(runs) // 2]
+    print(f"untraced step at ctx {CTX}: {statistics.median(plain) * 1e3:.1f} us (median of 5)")
+    print(tr.format_table(med))
+    print("attention sub-steps (median / max over CTAs, us): " +
+          ", ".join(f"{k} {a:.2f}/{b:.2f}" for k, (a, b) in med["_attn"].items()))
+
+
 def main():
     args = parse()
+    if args.case == "trace":
+        run_case_trace()
+        return
     if args.case == "small4":
         run_case_small4()
         return

@@ -157,8 +157,10 @@ int mk_decode_hidden(MkModel* m, const void* hidden_in, const int32_t* positions
  * must use mk_init / mk_decode. Runs on the current device. Its first call on
  * a device looks up the array's device address and sets the kernels'
  * shared-memory limit, so make that call before any stream capture. Each call
- * zeroes the counters it needs first. All calls on a device share the one
- * array, so calls that overlap on the GPU (other streams, other threads) race:
+ * zeroes the counters it needs first, and the array's activation words too
+ * when the geometry differs from the previous call's on that device (calls
+ * may alternate between models). All calls on a device share the one array,
+ * so calls that overlap on the GPU (other streams, other threads) race:
  * order them on one stream. Device-side failures are not reported by mk_sync:
  * pass error_out (device, 4 int32, zeroed by the call; code, detail, CTA,
  * thread on failure) or NULL.

@@ -69,7 +69,12 @@ struct MkModel {
   uint32_t* qkv = nullptr;
   uint32_t* attn = nullptr;
   uint32_t* act = nullptr;
-  uint32_t launch_seq = 0;   // launches so far: gives each launch its own tags
+  // Activation tags: the next launch's first tag, and the tagged words
+  // (h, qkv, attn, act: one contiguous range) zeroed before it would wrap.
+  uint32_t tag_next = 0;
+  void* act_words = nullptr;
+  size_t act_bytes = 0;
+  uint64_t xtag_next = 1;    // tensor-parallel exchange tags (32-bit, never 0)
   unsigned long long* partials = nullptr;  // attention split partials (tagged 64-bit words)
   size_t partials_bytes = 0;
   uint64_t part_tag_next = 0;  // partial tags used so far in the current tag sequence
@@ -175,7 +180,8 @@ int check_schedule_cached(const MkConfig* c, int B, int G, int S) {
 
 int validate_config(const MkConfig* c) {
   if (!c) return fail(MK_EINVAL, "config is NULL");
-  if (c->num_layers <= 0) return fail(MK_EINVAL, "num_layers must be > 0");
+  if (c->num_layers <= 0 || c->num_layers > 1024)
+    return fail(MK_EINVAL, "num_layers must be in [1, 1024] (got %d)", c->num_layers);
   if (c->head_dim != 64) return fail(MK_EINVAL, "head_dim must be 64 (got %d)", c->head_dim);
   if (c->num_kv_heads <= 0 || c->num_q_heads != 4 * c->num_kv_heads)
     return fail(MK_EINVAL, "num_q_heads must be 4 * num_kv_heads (got %d, %d)", c->num_q_heads,
@@ -309,9 +315,21 @@ int enqueue(MkModel* m, int mode, const int32_t* tokens, const int32_t* position
   p.host_error = m->host_error_dev;
   p.timeout_ns = m->timeout_ns;
   p.debug_skip_cta = m->debug_skip_cta;
-  // 5 tagged phases per layer plus the lm_head; tags stay distinct across
-  // the 65535 / (5 L + 1) launches before they repeat.
-  p.tag_base = (uint32_t)(((uint64_t)m->launch_seq++ * (uint64_t)(5 * c.num_layers + 1)) % 65535u);
+  // 5 tagged phases per layer plus the lm_head. A launch takes the next
+  // 5 L + 1 tags; before the counter would pass 65535 the tagged words are
+  // zeroed (0 is never a tag) and it restarts, so no word an earlier launch
+  // left behind, in rows this batch did not write then, can carry a tag of
+  // this launch.
+  const uint32_t span = (uint32_t)(5 * c.num_layers + 1);
+  if (m->tag_next + span > 65535u) {
+    MK_CUDA(cudaMemsetAsync(m->act_words, 0, m->act_bytes, static_cast<cudaStream_t>(stream)));
+    m->tag_next = 0;
+  }
+  p.tag_base = m->tag_next;
+  m->tag_next += span;
+  if (m->xtag_next + span >= 0xFFFFFFFFull) m->xtag_next = 1;
+  p.xtag_base = (uint32_t)m->xtag_next;
+  m->xtag_next += span;
   // Attention partials carry 32-bit tags of their own, one per layer and
   // launch, so a partial block that no split wrote this launch (the split
   // count follows the context) never matches: tags restart only after the
@@ -351,8 +369,12 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_mu;
 void* g_static_ptr[kStaticMaxDevices] = {};  // device address of g_static_scratch, per device
-uint32_t g_static_seq[kStaticMaxDevices] = {};  // launches so far per device (tags, see enqueue)
+uint32_t g_static_tag[kStaticMaxDevices] = {};   // next activation tag per device (see enqueue)
 uint64_t g_static_part[kStaticMaxDevices] = {};  // partial tags used per device (see enqueue)
+// The geometry of the last call on each device: calls may alternate between
+// models, and a call whose layout differs from the last one's would find that
+// call's tagged words at other offsets, so it starts from zeroed words.
+std::array<int, 8> g_static_geom[kStaticMaxDevices] = {};
 
 // Once per device, with that device current: the array's device address (the
 // host-side name g_static_scratch is only a stand-in and must never reach a
@@ -603,6 +625,8 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   m->qkv = reinterpret_cast<uint32_t*>(cb + o_qkv);
   m->attn = reinterpret_cast<uint32_t*>(cb + o_attn);
   m->act = reinterpret_cast<uint32_t*>(cb + o_act);
+  m->act_words = cb + o_h;
+  m->act_bytes = o_part - o_h;
   m->partials = reinterpret_cast<unsigned long long*>(cb + o_part);
   m->partials_bytes = part_bytes;
   m->counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
@@ -719,6 +743,8 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   m.qkv = reinterpret_cast<uint32_t*>(cb + o_qkv);
   m.attn = reinterpret_cast<uint32_t*>(cb + o_attn);
   m.act = reinterpret_cast<uint32_t*>(cb + o_act);
+  m.act_words = cb + o_h;
+  m.act_bytes = o_part - o_h;
   m.partials = reinterpret_cast<unsigned long long*>(cb + o_part);
   m.partials_bytes = part_bytes;
   m.counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
@@ -729,10 +755,21 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   m.host_error_dev = error_out ? reinterpret_cast<int*>(error_out) : reinterpret_cast<int*>(cb + o_mirror);
   rc = mk_load_weights(&m, w);
   if (rc) return rc;
-  bool restart = false;
+  bool restart = false, clear_words = false;
+  const uint32_t span = (uint32_t)(5 * cfg->num_layers + 1);
+  const std::array<int, 8> geom = {cfg->num_layers, cfg->hidden, cfg->intermediate,
+                                   cfg->num_q_heads, cfg->num_kv_heads, cfg->vocab, B, sms};
   {
     std::lock_guard<std::mutex> lock(g_static_mu);
-    m.launch_seq = g_static_seq[device]++;
+    // The activation tags of this call follow the last call's on this device;
+    // the words start from zero when the geometry changed or the tags wrap.
+    if (g_static_geom[device] != geom || g_static_tag[device] + span > 65535u) {
+      clear_words = true;
+      g_static_tag[device] = 0;
+      g_static_geom[device] = geom;
+    }
+    m.tag_next = g_static_tag[device];
+    g_static_tag[device] += span;
     m.part_tag_next = g_static_part[device];
     if (m.part_tag_next + cfg->num_layers >= kPartTagLimit) {
       m.part_tag_next = 0;
@@ -742,9 +779,11 @@ int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tok
   }
 
   // What must start at zero: barrier counters, argmax keys and error words
-  // (a previous call that failed on the device leaves them set), and the
+  // (a previous call that failed on the device leaves them set), the tagged
+  // activation words when the geometry changed or their tags wrap, and the
   // partials when their tag sequence restarts.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (clear_words) MK_CUDA(cudaMemsetAsync(cb + o_h, 0, o_part - o_h, st));
   if (restart) MK_CUDA(cudaMemsetAsync(m.partials, 0, m.partials_bytes, st));
   MK_CUDA(cudaMemsetAsync(cb + o_cnt, 0, o_mirror + 16 - o_cnt, st));
   if (error_out) MK_CUDA(cudaMemsetAsync(error_out, 0, 4 * sizeof(int32_t), st));

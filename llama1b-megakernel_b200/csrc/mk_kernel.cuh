@@ -25,18 +25,22 @@
 //   the epilogue (RoPE, KV scatter, SiLU*up, residual add) runs one thread
 //   per output, off the streaming loop.
 //
-// Phases per layer (grid barrier = acquire/release counter, time-bounded):
+// Phases per layer. There is no grid barrier: every activation a phase hands
+// to the next is written as tagged words (bf16 << 16 | a tag naming the launch
+// and the phase), and a consumer polls exactly the words it needs until they
+// carry the producing phase's tag (time-bounded).
 //   QKV    RMSNorm(h), q/k/v rows in RoPE pairs (d, d+32), llama3 RoPE from a
 //          bf16 cos/sin table, K/V row scattered into the paged cache.
 //   ATTN   split-K GQA flash-decode: item (seq, kv head, position range) per
-//          CTA, online softmax per warp, CTA merge, then the last CTA to
-//          finish a (seq, kv head) merges the splits plus the new token's own
-//          K/V and publishes the head (counter, no full barrier).
+//          CTA, online softmax per warp, CTA merge. A single split writes the
+//          heads' tagged output; with several, every split publishes tagged
+//          64-bit (o, m, l) partials and split 0, which also holds the new
+//          token's own K/V, merges them in split order and publishes.
 //   O      o_proj rows + residual add into h.
 //   GU     RMSNorm(h), gate/up row pairs, SiLU(gate) * up.
 //   DOWN   down rows + residual add into h.
 // then LM: final RMSNorm, lm_head rows, fp32 logits, packed 64-bit atomicMax
-// argmax; the last CTA to finish publishes the ids and resets the counters.
+// argmax; the last CTA to finish (an arrival counter) publishes the ids.
 //
 // Rounding mirrors HF Llama in bf16 (the reference's PyTorch path): every
 // linear output, RMSNorm output, RoPE product/sum, SiLU output, SwiGLU product
@@ -102,7 +106,14 @@ struct Params {
   int* host_error;           // [4] mapped pinned host mirror of `error`
   unsigned long long timeout_ns;
   int debug_skip_cta;
-  uint32_t tag_base;  // this launch's first tag (consecutive launches use disjoint tags)
+  // This launch's first activation tag. Tags only grow between two clears of
+  // the activation words (the host zeroes them before the counter would pass
+  // 65535), so no word left by an earlier launch carries a tag of this one.
+  uint32_t tag_base;
+  // First 32-bit tag of the tensor-parallel exchange words (peer-written, so
+  // never cleared by one rank alone): consecutive launches use disjoint
+  // ranges, and a range recurs only after 2^32 / (5 L + 1) launches.
+  uint32_t xtag_base;
   uint32_t part_tag0;  // layer 0's partial tag (layer l: + l); never 0, unique until the
                        // host zeroes the partials and restarts the sequence
   // optional phase trace ([grid][trace_per_cta] u64, see kTrace*); nullptr = off
@@ -221,6 +232,11 @@ __device__ __forceinline__ bool aborted(const Params& p) { return ld_volatile_i3
 
 __device__ __forceinline__ uint32_t phase_tag(const Params& p, int phase) {
   return 1u + (p.tag_base + (uint32_t)phase) % 65535u;
+}
+
+// The exchange-word tag of a phase (tensor parallelism only).
+__device__ __forceinline__ uint32_t xchg_tag(const Params& p, int phase) {
+  return p.xtag_base + (uint32_t)phase;
 }
 
 __device__ __forceinline__ uint32_t tagged(float v, uint32_t tag) {
@@ -1456,12 +1472,13 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       const int nu = so.u1 - so.u0, ns = p.nseg_qd;
       const uint32_t tag = phase_tag(p, l * 5 + 2);
       if (p.tp_world > 1) {
+        const uint32_t xtag = xchg_tag(p, l * 5 + 2);
         for (int i = tid; i < nu * B; i += kConsumerThreads)
-          tp_publish(p, 0, i % B, so.u0 + i / B, row_sum((i / B) * ns, ns, i % B), tag);
+          tp_publish(p, 0, i % B, so.u0 + i / B, row_sum((i / B) * ns, ns, i % B), xtag);
         int good = 1;
         for (int i = tid; i < nu * B && good; i += kConsumerThreads) {
           const int b = i % B, u = so.u0 + i / B;
-          const Summed o = tp_sum(p, 0, b, u, tag, 4500 + l);
+          const Summed o = tp_sum(p, 0, b, u, xtag, 4500 + l);
           good = o.ok;
           p.h[(size_t)b * H + u] = tagged(bf2f(raw[b * H + u]) + rbf(o.v), tag);
         }
@@ -1524,12 +1541,13 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       const int nu = sd.u1 - sd.u0, ns = p.nseg_i;
       const uint32_t tag = phase_tag(p, l * 5 + 4);
       if (p.tp_world > 1) {
+        const uint32_t xtag = xchg_tag(p, l * 5 + 4);
         for (int i = tid; i < nu * B; i += kConsumerThreads)
-          tp_publish(p, 1, i % B, sd.u0 + i / B, row_sum((i / B) * ns, ns, i % B), tag);
+          tp_publish(p, 1, i % B, sd.u0 + i / B, row_sum((i / B) * ns, ns, i % B), xtag);
         int good = 1;
         for (int i = tid; i < nu * B && good; i += kConsumerThreads) {
           const int b = i % B, u = sd.u0 + i / B;
-          const Summed d = tp_sum(p, 1, b, u, tag, 8500 + l);
+          const Summed d = tp_sum(p, 1, b, u, xtag, 8500 + l);
           good = d.ok;
           const float y = bf2f(raw[b * H + u]) + rbf(d.v);
           p.h[(size_t)b * H + u] = tagged(y, tag);
@@ -1610,7 +1628,7 @@ __device__ void run_consumers(const Params& p, SmemState& st, Ring& ring, bf16* 
       if (p.mode == 0) {
         unsigned long long key[B];
         for (int b = 0; b < B; ++b) key[b] = atomicExch(p.keys + b, 0ull);
-        if (p.tp_world == 1 || tp_argmax(p, key, phase_tag(p, p.L * 5))) {
+        if (p.tp_world == 1 || tp_argmax(p, key, xchg_tag(p, p.L * 5))) {
           for (int b = 0; b < B; ++b) {
             const int id = (int)(0xFFFFFFFFu - (uint32_t)(key[b] & 0xFFFFFFFFull));
             p.next_ids[b] = id;

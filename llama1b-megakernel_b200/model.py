@@ -258,7 +258,8 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int,
                  past_key_values: PagedKVCache | None = None,
                  prefill: bool = False, do_sample: bool = False, top_k: int = 1,
-                 top_p: float = 1.0, temperature: float = 1.0, seed: int = 0) -> torch.Tensor:
+                 top_p: float = 1.0, temperature: float = 1.0, seed: int = 0,
+                 cache_last: bool = False) -> torch.Tensor:
         """Greedy decoding: feed the prompt, then ``max_new_tokens`` steps on device.
 
         The prompt goes through the decode kernel one position per launch, or
@@ -271,6 +272,12 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         with ``top_k`` / ``top_p`` / ``temperature`` (draw s of the call uses
         step s of ``seed``) and feeds it back the same way. Returns
         [B, max_new_tokens] int64.
+
+        As with HF ``generate``, the cache ends holding the prompt and every
+        generated token but the last (whose K/V row no step has computed
+        yet); ``cache_last=True`` runs one more step to write that row too,
+        for a caller that continues from the cache (a whole 2.47 GB weight
+        stream for one K/V row).
         """
         kv = past_key_values if past_key_values is not None else self.kv
         if do_sample and self.lm_rows != self.cfg.vocab:
@@ -304,12 +311,13 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
             else:
                 self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
             result[:, s] = tok
-        self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
+        if cache_last:
+            self.launch(tok, pos, kv, None, self._next[:B], feedback=True)
         self.sync()
         if do_sample and int(self._sample_err[0]):
             self._sample_err.zero_()
             raise _lib.MkError(_lib.MK_EDEVICE, "sampling: more than 1024 logits tied at the top_k "
                                "threshold")
         for b in range(B):
-            kv.seq_lens[b] = int(start[b]) + max_new_tokens
+            kv.seq_lens[b] = int(start[b]) + max_new_tokens - (0 if cache_last else 1)
         return result.to(torch.int64)

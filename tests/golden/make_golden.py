@@ -1,9 +1,11 @@
 """Generate the committed golden fixtures under tests/golden/.
 
-Run from the repository root in the build container (it needs the reference
-checkout for the RoPE fixture):
+Run from the repository root; the RoPE fixture needs a checkout of the
+reference, named by the environment variable MK_REFERENCE_DIR (the directory
+holding its llama.py):
 
-    python tests/golden/make_golden.py rope      # rope_llama3.json
+    MK_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py rope
+                                                 # rope_llama3.json
     python tests/golden/make_golden.py greedy    # llama1b_greedy640.json (~1 min)
     python tests/golden/make_golden.py envelope  # adds the fp32 agreement (~20 min)
 
@@ -36,17 +38,25 @@ ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 
 HERE = Path(__file__).resolve().parent
-REFERENCE_LLAMA = Path(os.environ.get("MK_REFERENCE_DIR", "/root/reference")) / "llama.py"
 ROPE_POSITIONS = [0, 1, 2, 7, 63, 127, 128, 511, 767, 1023, 1024, 4095, 8191, 8192, 100000]
 
 
+def _reference_llama() -> Path:
+    d = os.environ.get("MK_REFERENCE_DIR")
+    if not d:
+        raise SystemExit("set MK_REFERENCE_DIR to the reference checkout (the directory holding "
+                         "its llama.py)")
+    return Path(d) / "llama.py"
+
+
 def _reference_rope_class():
-    src = REFERENCE_LLAMA.read_text()
+    ref = _reference_llama()
+    src = ref.read_text()
     tree = ast.parse(src)
     cls = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == "Llama3RotaryEmbedding")
     mod = ast.Module(body=[cls], type_ignores=[])
     ns = {"torch": torch, "nn": torch.nn, "math": math, "Optional": Optional}
-    exec(compile(mod, str(REFERENCE_LLAMA), "exec"), ns)
+    exec(compile(mod, str(ref), "exec"), ns)
     return ns["Llama3RotaryEmbedding"]
 
 

@@ -6,7 +6,12 @@ cache changes; per-step fp32 logits reach cosine >= 0.999 and max |diff| <=
 greedy ids match.
 
 Full-size Llama-3.2-1B with random-init weights is the exception to the
-max-abs bar, and the tests say why: in bf16 the reference's own path differs
+max-abs bar, and the tests show why with a second, independent bf16
+implementation: HF ``LlamaForCausalLM`` itself run in bf16 on the GPU
+(cuBLAS GEMMs, SDPA attention; test infrastructure, never the product).
+Its distance from the CPU reference is the spread that rounding order alone
+produces, and the kernel must be no farther from the reference than it
+(``SECOND_SLACK``), nor agree less often on greedy tokens. Further: in bf16 the reference's own path differs
 from exact (fp32) arithmetic on the same weights and cache by about 0.14 in
 max |logit| (16 layers of bf16 rounding on a residual that grows to |x| ~ 30
 against N(0,1) cached values), so any implementation that rounds in another
@@ -34,6 +39,8 @@ KV_ROW_TOL = 0.0625  # new K/V row values: a few bf16 ulps at |x| ~ 1
 ENVELOPE = 1.5       # 1B: kernel-to-fp32 distance <= ENVELOPE x reference-to-fp32
 MARGIN_SURE = 0.1    # 1B greedy: top-2 margin above which fp32 arithmetic agrees 100%
 DRIFT_MAX = 0.25     # 1B greedy: |kernel - reference| at the reference's top-1 logit
+SECOND_SLACK = 1.25  # 1B: kernel max|logit - reference| <= this x the second implementation's
+MATCH_SLACK = 0.01   # 1B greedy: kernel match rate >= second implementation's - this
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
@@ -76,6 +83,37 @@ def _check_logits(got, want, truth=None):
     return cos, err
 
 
+def _hf_gpu_model(cfg, w):
+    """HF LlamaForCausalLM in bf16 on cuda:0 (the second implementation)."""
+    return O.hf_model(cfg, {k: v for k, v in w.items() if not k.startswith("_")}).to("cuda:0")
+
+
+def _hf_gpu_logits(hf, w, hidden):
+    """The oracle's logit head (fp32 product of the tied embedding and the bf16
+    final-norm output) on HF's last hidden state [B, H]."""
+    e = w.get("_embed_f32_cuda")
+    if e is None:
+        e = w["_embed_f32_cuda"] = w["model.embed_tokens.weight"].to("cuda:0").float()
+    return hidden.float() @ e.t()
+
+
+def _hf_gpu_cache(hf, cfg, k, v):
+    from transformers import DynamicCache
+
+    cache = DynamicCache(config=hf.config)
+    for l in range(cfg.num_layers):
+        cache.update(k[l:l + 1].to("cuda:0"), v[l:l + 1].to("cuda:0"), l)
+    return cache
+
+
+@torch.no_grad()
+def _hf_gpu_step(hf, w, cache, tok, pos):
+    out = hf.model(input_ids=torch.tensor([[int(tok)]], device="cuda:0"),
+                   position_ids=torch.tensor([[int(pos)]], device="cuda:0"),
+                   past_key_values=cache, use_cache=True)
+    return _hf_gpu_logits(hf, w, out.last_hidden_state[:, -1]).cpu()
+
+
 def _check_argmax(got_ids, logits_ref, slack):
     for b in range(logits_ref.shape[0]):
         top2 = logits_ref[b].topk(2).values
@@ -83,11 +121,13 @@ def _check_argmax(got_ids, logits_ref, slack):
             assert int(got_ids[b]) == int(logits_ref[b].argmax()), b
 
 
-def _run_step_case(cfg, w, B, positions, page_size, seed, w32=None):
+def _run_step_case(cfg, w, B, positions, page_size, seed, w32=None, hf=None):
     """Fill random caches to positions[b], decode one step on GPU and oracle.
 
     With ``w32`` (fp32 weights) the step is also evaluated in fp32 and the
-    logits and the deeper layers' K/V rows are held to the envelope."""
+    logits and the deeper layers' K/V rows are held to the envelope. With
+    ``hf`` (the second implementation, B = 1) the kernel's max |logit -
+    reference| must be within SECOND_SLACK of HF-on-GPU's."""
     max_len = max(positions) + 1
     m = _model(cfg, w, B, max_seq_len=max_len + page_size, page_size=page_size, shuffle=seed)
     for b in range(B):
@@ -107,6 +147,16 @@ def _run_step_case(cfg, w, B, positions, page_size, seed, w32=None):
     cos, err = _check_logits(out.logits, ref["logits"],
                              truth["logits"] if truth is not None else None)
     _check_argmax(out.next_ids, ref["logits"], err.max().item())
+    if hf is not None:
+        assert B == 1
+        k, v = syn.random_kv_rows(cfg, positions[0], seed=seed, seq=0)
+        second = _hf_gpu_step(hf, w, _hf_gpu_cache(hf, cfg, k, v), toks[0], positions[0])
+        d_second = (second - ref["logits"]).abs().max().item()
+        cos_second = torch.nn.functional.cosine_similarity(second, ref["logits"], dim=-1).item()
+        d_kernel = err.max().item()
+        print(f"pos {positions[0]}: max|kernel-ref| {d_kernel:.4f} (cos {cos.min().item():.6f}), "
+              f"max|hf_gpu-ref| {d_second:.4f} (cos {cos_second:.6f})")
+        assert d_kernel <= SECOND_SLACK * d_second + 1e-3, (d_kernel, d_second)
     # KV scatter: exactly the rows at `positions` changed, with the oracle's values.
     ps = page_size
     changed = (m.kv.k_pages != before_k) | (m.kv.v_pages != before_v)
@@ -253,15 +303,25 @@ def llama_w32(llama_w):
     return _fp32_copy(llama_w)
 
 
+@pytest.fixture(scope="module")
+def llama_hf_gpu(llama_w):
+    hf = _hf_gpu_model(LLAMA_3_2_1B, llama_w)
+    yield hf
+    del hf
+    llama_w.pop("_embed_f32_cuda", None)
+    torch.cuda.empty_cache()
+
+
 @pytest.mark.parametrize("ctx", [128, 1024, 4096, 8192])
-def test_llama1b_single_step_ctx(llama_w, llama_w32, ctx):
-    """One step at position ctx over ctx cached N(0,1) rows (the context sweep)."""
+def test_llama1b_single_step_ctx(llama_w, llama_w32, llama_hf_gpu, ctx):
+    """One step at position ctx over ctx cached N(0,1) rows (the context sweep),
+    held to the fp32 envelope and to the second implementation's distance."""
     m, out, ref = _run_step_case(LLAMA_3_2_1B, llama_w, 1, [ctx], page_size=64, seed=ctx,
-                                 w32=llama_w32)
+                                 w32=llama_w32, hf=llama_hf_gpu)
     del m
 
 
-def test_llama1b_greedy_640_teacher_forced(llama_w, llama_w32):
+def test_llama1b_greedy_640_teacher_forced(llama_w, llama_w32, llama_hf_gpu):
     """128-token prompt, then 640 greedy steps (the bench workload).
 
     The kernel is fed the oracle's greedy tokens (teacher forcing, as the
@@ -279,6 +339,9 @@ def test_llama1b_greedy_640_teacher_forced(llama_w, llama_w32):
     disagreements all have margins under 0.08), and
     (b) agree overall at no less than the fp32 evaluation's rate minus 2%.
     A 99% bar applies where the reference's decisions are not within noise.
+    (c) The second implementation (HF in bf16 on the GPU), teacher-forced the
+    same way, sets the overall bar: the kernel must agree with the reference
+    at no less than its rate minus MATCH_SLACK.
     """
     d = json.loads((GOLDEN / "llama1b_greedy640.json").read_text())
     from tests.golden.make_golden import weight_fingerprint
@@ -312,15 +375,34 @@ def test_llama1b_greedy_640_teacher_forced(llama_w, llama_w32):
             truth = O.decode_step(cfg, llama_w32, kv32, [feed[s]], [pos0 + s])
             _check_logits(logits, ref["logits"], truth["logits"])
     m.sync()
+    # The second implementation: HF bf16 on the GPU, the prompt prefilled in
+    # one forward, then the same teacher-forced tokens one step at a time.
+    with torch.no_grad():
+        from transformers import DynamicCache
+
+        hf = llama_hf_gpu
+        cache = DynamicCache(config=hf.config)
+        hf.model(input_ids=prompt[:, :-1].to("cuda:0"), past_key_values=cache, use_cache=True)
+        hf_ids, hf_top1 = [], []
+        for s_ in range(640):
+            lg = _hf_gpu_step(hf, llama_w, cache, feed[s_], pos0 + s_)[0]
+            hf_ids.append(int(lg.argmax()))
+            hf_top1.append(float(lg[int(want_ids[s_])]))
+    hf_same = torch.tensor(hf_ids) == want_ids.cpu()
+    hf_match = hf_same.float().mean().item()
+    hf_drift = (torch.tensor(hf_top1) - want_top1.cpu()).abs().max().item()
     same = (got.long() == want_ids).cpu()
     match = same.float().mean().item()
     drift = (top1 - want_top1).abs().max().item()
     top2 = torch.tensor([[float.fromhex(v) for v in r] for r in d["top2_logits_f32_hex"]])
     margin = top2[:, 0] - top2[:, 1]
     sure = margin > MARGIN_SURE
-    print(f"greedy match {match:.4f} (fp32 evaluation {d['fp32_teacher_forced_match']:.4f}), "
-          f"steps with margin > {MARGIN_SURE}: {int(sure.sum())}, matched "
-          f"{int(same[sure].sum())}; max |top1 logit - fixture| {drift:.4f}")
+    print(f"greedy match {match:.4f} (fp32 evaluation {d['fp32_teacher_forced_match']:.4f}, "
+          f"HF bf16 on the GPU {hf_match:.4f}), steps with margin > {MARGIN_SURE}: "
+          f"{int(sure.sum())}, matched {int(same[sure].sum())} (HF GPU "
+          f"{int(hf_same[sure].sum())}); max |top1 logit - fixture| {drift:.4f} "
+          f"(HF GPU {hf_drift:.4f})")
     assert same[sure].float().mean().item() >= 0.99
     assert match >= d["fp32_teacher_forced_match"] - 0.02
+    assert match >= hf_match - MATCH_SLACK
     assert drift <= DRIFT_MAX

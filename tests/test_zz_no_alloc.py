@@ -16,7 +16,7 @@ import torch
 
 from llama1b_megakernel_b200 import _lib
 from llama1b_megakernel_b200 import synthetic as syn
-from llama1b_megakernel_b200.config import SMALL
+from llama1b_megakernel_b200.config import LLAMA_3_2_1B, SMALL, TINY
 
 pytestmark = pytest.mark.gpu
 
@@ -51,6 +51,32 @@ def small_model():
     w = syn.make_weights(SMALL, seed=31)
     return MegakernelLlamaForCausalLM(SMALL, w, max_batch=1, max_seq_len=256, page_size=32,
                                       device="cuda:0")
+
+
+def _model(cfg, seed, max_seq_len, page_size):
+    from llama1b_megakernel_b200.model import MegakernelLlamaForCausalLM
+
+    w = syn.make_weights(cfg, seed=seed, device="cuda:0")
+    return MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=max_seq_len,
+                                      page_size=page_size, device="cuda:0")
+
+
+def _compare_steps(m, kv_ref, kv_st, tok, pos, err, what):
+    """One step through mk_decode (kv_ref) and mk_decode_static (kv_st)."""
+    dev = m.device
+    lg_ref = torch.empty(1, m.cfg.vocab, dtype=torch.float32, device=dev)
+    lg_st = torch.empty_like(lg_ref)
+    id_ref = torch.empty(1, dtype=torch.int32, device=dev)
+    id_st = torch.empty_like(id_ref)
+    m.launch(tok, pos, kv_ref, lg_ref, id_ref)
+    m.sync()
+    _static_step(m, kv_st, tok, pos, lg_st, id_st, err)
+    torch.cuda.synchronize()
+    assert err.tolist() == [0, 0, 0, 0], what
+    cos = torch.nn.functional.cosine_similarity(lg_st, lg_ref, dim=-1).item()
+    diff = (lg_st - lg_ref).abs().max().item()
+    assert cos >= COS_MIN and diff <= MAXABS, (what, cos, diff)
+    assert int(id_st[0]) == int(id_ref[0]), what
 
 
 def _filled_cache(m, n, seed):
@@ -121,3 +147,43 @@ def test_static_rejects_geometry_beyond_the_array(small_model):
                                 None, torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.MK_EINVAL
     assert "static array" in m.lib.mk_last_error().decode()
+
+
+def test_static_at_llama_1b_geometry():
+    """Llama-3.2-1B at max_batch 1, the geometry the static array is sized
+    for: two consecutive steps at ctx 1024 against mk_decode."""
+    m = _model(LLAMA_3_2_1B, seed=0, max_seq_len=1088, page_size=64)
+    n = 1024
+    kv_ref, kv_st = _filled_cache(m, n, seed=11), _filled_cache(m, n, seed=11)
+    toks = syn.random_tokens(2, m.cfg.vocab, seed=12).to(torch.int32)
+    err = torch.full((4,), -1, dtype=torch.int32, device=m.device)
+    for step in range(2):
+        tok = toks[step:step + 1].to(m.device)
+        pos = torch.tensor([n + step], dtype=torch.int32, device=m.device)
+        _compare_steps(m, kv_ref, kv_st, tok, pos, err, f"1B step {step}")
+    k_ref, v_ref = kv_ref.gather(0, n + 2)
+    k_st, v_st = kv_st.gather(0, n + 2)
+    assert torch.equal(k_ref, k_st) and torch.equal(v_ref, v_st)
+    del m, kv_ref, kv_st
+    torch.cuda.empty_cache()
+
+
+def test_static_alternating_geometries():
+    """Calls that alternate between two models of different depth and width
+    share the one static array; each step must still equal its own model's
+    handle-based mk_decode step (stale words of the other model's layout
+    must never pass for this call's activations)."""
+    tiny = _model(TINY, seed=41, max_seq_len=128, page_size=16)
+    small = _model(SMALL, seed=42, max_seq_len=128, page_size=32)
+    caches = {}
+    for name, m in (("tiny", tiny), ("small", small)):
+        caches[name] = (_filled_cache(m, 40, seed=43), _filled_cache(m, 40, seed=43))
+    err = torch.full((4,), -1, dtype=torch.int32, device=tiny.device)
+    for step in range(6):
+        for name, m in (("tiny", tiny), ("small", small)):
+            kv_ref, kv_st = caches[name]
+            tok = torch.tensor([(17 * step + 5) % m.cfg.vocab], dtype=torch.int32, device=m.device)
+            pos = torch.tensor([40 + step], dtype=torch.int32, device=m.device)
+            for c in (kv_ref, kv_st):
+                c.reserve(0, 40 + step + 1)
+            _compare_steps(m, kv_ref, kv_st, tok, pos, err, f"{name} step {step}")
