@@ -458,6 +458,9 @@ def run_ours(args, ws, rank, local):
     batched_res = None
     if sweep and not args.no_batched:
         batched_res = run_batched(model, cfg, dev, hbm_peak)
+    tp_bs32 = None
+    if tp_world > 1 and not (args.no_batched or args.small):
+        tp_bs32 = run_tp_batched(model, cfg, dev, ws)
 
     # ------------------------------------------------------------ cpu baseline (config 1)
     cpu_b = None
@@ -500,6 +503,8 @@ def run_ours(args, ws, rank, local):
             line["ctx_sweep"] = sweep_res
         if batched_res is not None:
             line["batched"] = batched_res
+        if tp_bs32 is not None:
+            line["tp_bs32"] = tp_bs32
         if cpu_b is not None:
             line["cpu_baseline"] = cpu_b
         print(json.dumps(line), flush=True)
@@ -541,6 +546,41 @@ def run_batched(model, cfg, dev, hbm_peak):
     del dec
     torch.cuda.empty_cache()
     return res
+
+
+def run_tp_batched(model, cfg, dev, ws, B: int = 32, L: int = 1024):
+    """BASELINE config 5 at bs 32: the batched step on every rank of the
+    tensor-parallel group (BatchedDecoder on the TP model: shard GEMMs, NCCL
+    all-reduce of the o_proj / down partial sums inside the graph), KV length
+    1024 per sequence. Step time = median of 20 graph replays, max over ranks."""
+    from llama1b_megakernel_b200 import synthetic as syn
+    from llama1b_megakernel_b200.batched import BatchedDecoder
+
+    dec = BatchedDecoder(model, max_batch=B, max_seq_len=L + 64, page_size=64)
+    nkv = model.cfg.num_kv_heads
+    g0 = model.tp_rank * nkv
+    for b in range(B):
+        k, v = syn.random_kv_rows(cfg, L, seed=100 + b, seq=b, device=dev)
+        dec.kv.fill(b, k[:, g0:g0 + nkv], v[:, g0:g0 + nkv])
+        del k, v
+    dec.step(syn.random_tokens(B, cfg.vocab, seed=B), torch.full((B,), L, dtype=torch.int32))
+    for _ in range(3):
+        dec.replay(B)
+    torch.cuda.synchronize()
+    barrier(ws)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(21)]
+    ev[0].record()
+    for j in range(20):
+        dec.replay(B)
+        ev[j + 1].record()
+    torch.cuda.synchronize()
+    dec.check()
+    med = max_over_ranks(statistics.median(ev[j].elapsed_time(ev[j + 1]) for j in range(20)), ws)
+    del dec
+    torch.cuda.empty_cache()
+    return {"batch": B, "kv_len": L, "ms_p50": med, "tok_s": B * 1e3 / med,
+            "gemm": "mk_gemm_bf16 (tcgen05) on each rank's shard",
+            "collective": "NCCL all-reduce (fp32 partial sums) x 2 per layer inside the CUDA graph"}
 
 
 def run_case_gemm():

@@ -253,7 +253,7 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
  * Y[rows][n] = X[rows][k] . W[n][k]^T (+ residual[rows][n]), bf16 inputs,
  * fp32 accumulation, Y bf16 (out) or fp32 (out_f32, no residual). W is a
  * weight matrix in HF [out][in] layout (any n, k a multiple of 64); X has
- * rows_padded (16, 32 or 64) rows of which the first `rows` are real and the
+ * rows_padded (16, 32, 64, or 128 for prompt prefill) rows of which the first `rows` are real and the
  * rest zero. Narrow W is split along k over the CTAs of a thread-block
  * cluster whose partial sums meet in distributed shared memory, so no
  * workspace is needed: mk_gemm_workspace returns 0 and `workspace` may be
@@ -293,6 +293,28 @@ int mk_swiglu(const void* gate_up, int64_t n, void* out, void* stream);
  * the reference's greedy sampling takes the argmax of the logits
  * (llama.py:1208-1227, torch.argmax). Asynchronous. */
 int mk_argmax_rows(const float* x, int32_t rows, int32_t cols, int64_t* ids, void* stream);
+
+/* ---- Tensor-parallel batched step ------------------------------------------
+ *
+ * The reference's baseline decoder shards o_proj and down by their input
+ * columns (RowParallelLinear, llama.py:437-470) and all-reduces their
+ * outputs; its lm_head is vocabulary-parallel with the logits gathered for
+ * the greedy argmax (llama.py:1208-1227). With the rank's partial sums of
+ * o_proj / down all-reduced into `sum` ([rows][hidden] fp32):
+ * mk_add_rmsnorm_rows: x = bf16(x + bf16(sum)) in place (the decoder layer's
+ *   residual add), out = bf16(bf16(x * 1/sqrt(mean(x^2) + eps)) * gamma).
+ * mk_argmax_keys: per row of this rank's fp32 logits [rows][cols] (vocabulary
+ *   ids id0 .. id0 + cols - 1), the key (order-preserving float bits of the
+ *   maximum << 32 | 2^32 - 1 - the id of its first occurrence), so that the
+ *   integer maximum of the ranks' keys names the global greedy id with the
+ *   lowest index on ties.
+ * mk_keys_to_ids: keys [world][rows] (gathered from every rank) -> ids [rows].
+ * All asynchronous on `stream`. */
+int mk_add_rmsnorm_rows(void* x, const float* sum, const void* gamma, float eps, int32_t rows,
+                        int32_t hidden, void* out, void* stream);
+int mk_argmax_keys(const float* x, int32_t rows, int32_t cols, int32_t id0, uint64_t* keys,
+                   void* stream);
+int mk_keys_to_ids(const uint64_t* keys, int32_t world, int32_t rows, int64_t* ids, void* stream);
 
 /* ---- Tensor parallelism (one decode step over `world` GPUs) --------------
  *

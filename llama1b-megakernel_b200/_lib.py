@@ -25,7 +25,8 @@ EXPORTED = (
     "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_schedule_gap", "mk_sample", "mk_paged_attention_workspace",
-    "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_argmax_rows", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
+    "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_argmax_rows",
+    "mk_add_rmsnorm_rows", "mk_argmax_keys", "mk_keys_to_ids", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
     "mk_destroy",
 )
 
@@ -94,8 +95,8 @@ def load() -> ctypes.CDLL:
     lib.mk_set_timeout_ns.argtypes = [VP, ctypes.c_uint64]
     lib.mk_debug_skip_arrival.argtypes = [VP, I32]
     lib.mk_set_trace.argtypes = [VP, VP, ctypes.c_int64, P(ctypes.c_int64)]
-    lib.mk_query.argtypes = [VP, P(I32), P(I32), P(I32)]
     lib.mk_schedule_gap.argtypes = [P(MkConfig), I32, I32, P(I32)]
+    lib.mk_query.argtypes = [VP, P(I32), P(I32), P(I32)]
     lib.mk_sample.argtypes = [VP, I32, I32, ctypes.c_int64, P(MkSampling), ctypes.c_uint64,
                               ctypes.c_uint64, VP, VP, VP, VP, VP]
     lib.mk_paged_attention_workspace.argtypes = [I32, I32, I32]
@@ -110,6 +111,9 @@ def load() -> ctypes.CDLL:
                                     VP, VP]
     lib.mk_swiglu.argtypes = [VP, ctypes.c_int64, VP, VP]
     lib.mk_argmax_rows.argtypes = [VP, I32, I32, VP, VP]
+    lib.mk_add_rmsnorm_rows.argtypes = [VP, VP, VP, ctypes.c_float, I32, I32, VP, VP]
+    lib.mk_argmax_keys.argtypes = [VP, I32, I32, I32, VP, VP]
+    lib.mk_keys_to_ids.argtypes = [VP, I32, I32, VP, VP]
     lib.mk_tp_setup.argtypes = [VP, I32, I32, I32, I32, P(MkIpcHandle), P(VP)]
     lib.mk_tp_connect.argtypes = [VP, P(MkIpcHandle), P(VP)]
     lib.mk_last_error.argtypes = []

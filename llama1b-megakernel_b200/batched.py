@@ -21,16 +21,27 @@ path runs one step as:
 * the whole step is captured once per batch size into a CUDA graph, so a step
   is one graph launch with the tokens and positions on the device.
 
-Rounding follows HF's decode step in bf16 (as the prefill path does), except
-that a residual add happens inside the GEMM's fp32 epilogue (one bf16
-rounding of x + W a instead of two); the attention output is rounded to bf16
-from fp32 softmax sums (as the megakernel does).
+Tensor parallelism (``model`` a ``TensorParallelLlamaForCausalLM``; BASELINE
+config 5 at bs 32): each rank holds its q / kv heads, MLP rows and lm_head
+rows (tp.py). The q/k/v and gate/up GEMMs, RoPE, the KV cache and attention
+are local; o_proj and down produce fp32 partial sums over the rank's input
+columns (RowParallelLinear, llama.py:437-470), which an NCCL all-reduce sums
+inside the captured graph, and ``mk_add_rmsnorm_rows`` adds the sum to the
+residual and normalises for the next GEMM. The lm_head scores the rank's
+vocabulary rows; ``mk_argmax_keys`` packs each row's maximum and global id
+into one integer key, the keys are all-gathered and ``mk_keys_to_ids`` takes
+the largest (lowest id on ties).
+
+Rounding follows HF's decode step in bf16 (the GEMM epilogue rounds W a to
+bf16 before the residual add, and the sum again); the attention output is
+rounded to bf16 from fp32 softmax sums (as the megakernel does).
 """
 from __future__ import annotations
 
 import ctypes
 
 import torch
+import torch.distributed as dist
 
 from . import _lib
 from .kv_cache import PagedKVCache
@@ -38,12 +49,14 @@ from .kv_cache import PagedKVCache
 
 class BatchedDecoder:
     """Greedy decode steps for up to ``max_batch`` sequences with the weights
-    of ``model`` (a ``MegakernelLlamaForCausalLM``; single GPU)."""
+    of ``model``: a ``MegakernelLlamaForCausalLM`` (one GPU) or one rank of a
+    ``TensorParallelLlamaForCausalLM`` (every rank of its group constructs
+    the decoder and makes the same calls in the same order)."""
 
     def __init__(self, model, max_batch: int, max_seq_len: int, page_size: int = 64,
                  num_pages: int | None = None):
-        if getattr(model, "tp_world", 1) != 1:
-            raise NotImplementedError("the batched path runs on one GPU")
+        self.tp_world = getattr(model, "tp_world", 1)
+        self.group = getattr(model, "tp_group", None)
         if not 1 <= max_batch <= 64:
             raise ValueError(f"max_batch {max_batch} outside [1, 64] (the GEMM's padded batch)")
         if max_seq_len > model.rope_len:
@@ -94,11 +107,18 @@ class BatchedDecoder:
         BP = 16 if B <= 16 else 32 if B <= 32 else 64
         nh = c.num_q_heads + 2 * c.num_kv_heads
         z = lambda *shape: torch.zeros(*shape, dtype=torch.bfloat16, device=dev)  # noqa: E731
-        return dict(x=z(B, c.hidden), h=z(BP, c.hidden), q=z(B, c.num_q_heads, 64),
-                    attn=z(BP, c.num_q_heads * 64), act=z(BP, c.intermediate),
-                    qkv=z(B, nh * 64), gu=z(B, 2 * c.intermediate))
+        buf = dict(x=z(B, c.hidden), h=z(BP, c.hidden), q=z(B, c.num_q_heads, 64),
+                   attn=z(BP, c.num_q_heads * 64), act=z(BP, c.intermediate),
+                   qkv=z(B, nh * 64), gu=z(B, 2 * c.intermediate))
+        if self.tp_world > 1:
+            buf["part"] = torch.zeros(B, c.hidden, dtype=torch.float32, device=dev)
+            buf["keys"] = torch.zeros(B, dtype=torch.int64, device=dev)
+            buf["keys_all"] = torch.zeros(self.tp_world * B, dtype=torch.int64, device=dev)
+        return buf
 
     def _step(self, tokens, positions, logits_out, ids_out, buf):
+        if self.tp_world > 1:
+            return self._step_tp(tokens, positions, logits_out, ids_out, buf)
         c, pw, kv, lib = self.cfg, self.m.packed, self.kv, self.lib
         B = tokens.numel()
         H, NQ, NKV, I = c.hidden, c.num_q_heads, c.num_kv_heads, c.intermediate
@@ -128,13 +148,56 @@ class BatchedDecoder:
         self._gemm(pw.embed, h, B, out_f32=logits_out)
         _lib.check(lib.mk_argmax_rows(logits_out.data_ptr(), B, c.vocab, ids_out.data_ptr(), st))
 
+    def _step_tp(self, tokens, positions, logits_out, ids_out, buf):
+        """One step on this rank of a tensor-parallel group (see the module
+        docstring); every rank runs the same kernels and collectives."""
+        c, pw, kv, lib, m = self.cfg, self.m.packed, self.kv, self.lib, self.m
+        B = tokens.numel()
+        H, NQ, NKV, I, L = c.hidden, c.num_q_heads, c.num_kv_heads, c.intermediate, c.num_layers
+        st = torch.cuda.current_stream().cuda_stream
+        x, h, q, attn, act, qkv, gu = (buf[k] for k in ("x", "h", "q", "attn", "act", "qkv", "gu"))
+        part, keys, keys_all = buf["part"], buf["keys"], buf["keys_all"]
+        x.copy_(pw.embed[tokens.long()])
+        lengths = (positions + 1).to(torch.int32)
+        eps = ctypes.c_float(c.rms_eps)
+        _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_attn[0].data_ptr(), eps, B, H,
+                                       h.data_ptr(), st))
+        for l in range(L):
+            self._gemm(pw.w_qkv[l].view(-1, H), h, B, out=qkv)
+            _lib.check(lib.mk_rope_scatter(
+                qkv.data_ptr(), pw.rope_cos.data_ptr(), pw.rope_sin.data_ptr(),
+                positions.data_ptr(), kv.block_tables.data_ptr(), kv.max_blocks, kv.num_pages,
+                kv.page_size, NQ, NKV, B, q.data_ptr(), kv.k_pages[l].data_ptr(),
+                kv.v_pages[l].data_ptr(), self.err.data_ptr(), st))
+            self._attention(q, l, lengths, B, attn)
+            self._gemm(pw.w_o[l], attn, B, out_f32=part)  # this rank's partial o_proj
+            dist.all_reduce(part, group=self.group)
+            _lib.check(lib.mk_add_rmsnorm_rows(x.data_ptr(), part.data_ptr(),
+                                               pw.norm_mlp[l].data_ptr(), eps, B, H,
+                                               h.data_ptr(), st))
+            self._gemm(pw.w_gate_up[l].view(2 * I, H), h, B, out=gu)
+            _lib.check(lib.mk_swiglu(gu.data_ptr(), B * I, act.data_ptr(), st))
+            self._gemm(pw.w_down[l], act, B, out_f32=part)  # this rank's partial down
+            dist.all_reduce(part, group=self.group)
+            gamma = pw.norm_attn[l + 1] if l + 1 < L else pw.norm_final
+            _lib.check(lib.mk_add_rmsnorm_rows(x.data_ptr(), part.data_ptr(), gamma.data_ptr(),
+                                               eps, B, H, h.data_ptr(), st))
+        row0, rows = m.lm_row0, m.lm_rows
+        self._gemm(pw.embed[row0:row0 + rows], h, B, out_f32=logits_out)
+        _lib.check(lib.mk_argmax_keys(logits_out.data_ptr(), B, rows, row0, keys.data_ptr(), st))
+        dist.all_gather_into_tensor(keys_all, keys, group=self.group)
+        _lib.check(lib.mk_keys_to_ids(keys_all.data_ptr(), self.tp_world, B, ids_out.data_ptr(),
+                                      st))
+
     def _graph(self, B: int):
         g = self._graphs.get(B)
         if g is None:
             dev = self.dev
             tok = torch.zeros(B, dtype=torch.int32, device=dev)
             pos = torch.zeros(B, dtype=torch.int32, device=dev)
-            logits = torch.empty(B, self.cfg.vocab, dtype=torch.float32, device=dev)
+            # this rank's lm_head rows (the whole vocabulary on one GPU)
+            logits = torch.empty(B, getattr(self.m, "lm_rows", self.cfg.vocab),
+                                 dtype=torch.float32, device=dev)
             ids = torch.empty(B, dtype=torch.int64, device=dev)
             buf = self._buffers(B)
             # warm up on a side stream, then capture. The warm-up really runs
@@ -163,7 +226,9 @@ class BatchedDecoder:
     def step(self, tokens: torch.Tensor, positions: torch.Tensor):
         """One greedy step for len(tokens) sequences (row b = cache slot b), K/V
         written at ``positions``; returns (logits [B, V] fp32, ids [B] int64),
-        views of the step's static buffers (valid until the next step)."""
+        views of the step's static buffers (valid until the next step). On a
+        tensor-parallel rank the logits are the rank's vocabulary rows
+        (``tp.gather_slices`` assembles them) and the ids are global."""
         B = int(tokens.numel())
         if B > self.max_batch:
             raise ValueError(f"batch {B} > {self.max_batch}")

@@ -941,8 +941,8 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
     return fail(MK_EINVAL, "w, x, error and exactly one of out / out_f32 are required");
   if (n < 1 || k < mk::kGemmTileK || k % mk::kGemmTileK)
     return fail(MK_EINVAL, "k must be a positive multiple of 64 and n positive (n %d, k %d)", n, k);
-  if (rows_padded != 16 && rows_padded != 32 && rows_padded != 64)
-    return fail(MK_EINVAL, "rows_padded must be 16, 32 or 64 (got %d)", rows_padded);
+  if (rows_padded != 16 && rows_padded != 32 && rows_padded != 64 && rows_padded != 128)
+    return fail(MK_EINVAL, "rows_padded must be 16, 32, 64 or 128 (got %d)", rows_padded);
   if (rows < 1 || rows > rows_padded) return fail(MK_EINVAL, "rows %d outside [1, %d]", rows, rows_padded);
   if (!aligned16(w) || !aligned16(x)) return fail(MK_EINVAL, "w and x must be 16-byte aligned");
   if (residual && out_f32) return fail(MK_EINVAL, "a residual needs the bf16 output");
@@ -970,7 +970,8 @@ int mk_gemm_bf16(const void* w, int32_t n, int32_t k, const void* x, int32_t row
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = rows_padded == 16 ? launch_gemm<16>(gp, tiles, splits, st)
                   : rows_padded == 32 ? launch_gemm<32>(gp, tiles, splits, st)
-                                      : launch_gemm<64>(gp, tiles, splits, st);
+                  : rows_padded == 64 ? launch_gemm<64>(gp, tiles, splits, st)
+                                      : launch_gemm<128>(gp, tiles, splits, st);
   if (e != cudaSuccess) return fail(MK_ECUDA, "gemm launch: %s", cudaGetErrorString(e));
   return MK_OK;
 }
@@ -1013,6 +1014,36 @@ int mk_argmax_rows(const float* x, int32_t rows, int32_t cols, int64_t* ids, voi
   const bool vec = cols % 4 == 0 && aligned16(x);
   MK_CUDA(launch_pdl(mk::argmax_rows_kernel, dim3(rows), dim3(1024), 0,
                      static_cast<cudaStream_t>(stream), x, (int)cols, vec, ids));
+  return MK_OK;
+}
+
+int mk_add_rmsnorm_rows(void* x, const float* sum, const void* gamma, float eps, int32_t rows,
+                        int32_t hidden, void* out, void* stream) {
+  if (!x || !sum || !gamma || !out) return fail(MK_EINVAL, "NULL argument");
+  if (rows < 1 || hidden < 8 || hidden % 8) return fail(MK_EINVAL, "rows %d, hidden %d", rows, hidden);
+  if (!aligned16(x) || !aligned16(sum) || !aligned16(gamma) || !aligned16(out))
+    return fail(MK_EINVAL, "16-byte alignment");
+  MK_CUDA(launch_pdl(mk::add_rmsnorm_rows_kernel, dim3(rows), dim3(256), 0,
+                     static_cast<cudaStream_t>(stream), static_cast<mk::bf16*>(x), sum,
+                     static_cast<const mk::bf16*>(gamma), eps, (int)hidden, static_cast<mk::bf16*>(out)));
+  return MK_OK;
+}
+
+int mk_argmax_keys(const float* x, int32_t rows, int32_t cols, int32_t id0, uint64_t* keys,
+                   void* stream) {
+  if (!x || !keys || rows < 1 || cols < 1 || id0 < 0)
+    return fail(MK_EINVAL, "argmax keys: x, keys, rows >= 1, cols >= 1 and id0 >= 0 are required");
+  MK_CUDA(launch_pdl(mk::argmax_keys_kernel, dim3(rows), dim3(1024), 0,
+                     static_cast<cudaStream_t>(stream), x, (int)cols, (int)id0,
+                     reinterpret_cast<unsigned long long*>(keys)));
+  return MK_OK;
+}
+
+int mk_keys_to_ids(const uint64_t* keys, int32_t world, int32_t rows, int64_t* ids, void* stream) {
+  if (!keys || !ids || world < 1 || rows < 1) return fail(MK_EINVAL, "keys to ids: arguments");
+  MK_CUDA(launch_pdl(mk::keys_to_ids_kernel, dim3((rows + 127) / 128), dim3(128), 0,
+                     static_cast<cudaStream_t>(stream),
+                     reinterpret_cast<const unsigned long long*>(keys), (int)world, (int)rows, ids));
   return MK_OK;
 }
 

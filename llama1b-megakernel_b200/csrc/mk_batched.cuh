@@ -10,6 +10,10 @@
 //             cos/sin table rows of the step's positions
 //   swiglu:   a = bf16(bf16(g / (1 + exp(-g))) * u)
 //   argmax:   the greedy id of each row of fp32 logits (lowest index on ties)
+// and, for the tensor-parallel batched step:
+//   add + rmsnorm: x = bf16(x + bf16(partial sum)), then rmsnorm(x)
+//   argmax keys:   (order-preserving float bits << 32 | ~global id) per row,
+//                  so the ranks' keys combine by an integer max
 #pragma once
 
 #include <cuda_bf16.h>
@@ -183,6 +187,127 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* x, int c
     }
     if (lane == 0) ids[blockIdx.x] = idx == 0x7fffffff ? 0 : idx;
   }
+}
+
+// Tensor parallelism, after the o_proj / down partial sums of every rank
+// were summed into `sum` ([B][H] fp32): x = bf16(x + bf16(sum)) in place (the
+// residual add of HF's decoder layer on the all-reduced projection), then
+// y = rmsnorm(x) with gamma. One CTA of 256 threads per row; H a multiple of 8.
+__global__ void __launch_bounds__(256) add_rmsnorm_rows_kernel(__nv_bfloat16* x, const float* sum,
+                                                               const __nv_bfloat16* gamma,
+                                                               float eps, int H,
+                                                               __nv_bfloat16* y) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[8];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  uint4* xr = reinterpret_cast<uint4*>(x + (size_t)b * H);
+  const float4* sr = reinterpret_cast<const float4*>(sum + (size_t)b * H);
+  float ss = 0.f;
+  for (int i = tid; i < H / 8; i += 256) {
+    const uint4 u = xr[i];
+    const float4 s0 = sr[2 * i], s1 = sr[2 * i + 1];
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bfr(__uint_as_float(w[e] << 16) + bfr(sv[2 * e]));
+      const float hi = bfr(__uint_as_float(w[e] & 0xFFFF0000u) + bfr(sv[2 * e + 1]));
+      ss = fmaf(lo, lo, ss);
+      ss = fmaf(hi, hi, ss);
+      __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+      o[e] = *reinterpret_cast<uint32_t*>(&pr);
+    }
+    xr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w];
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), eps)));
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)b * H);
+  for (int i = tid; i < H / 8; i += 256) {
+    const uint4 u = xr[i], g = gr[i];  // this thread's own x words, written above
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w}, gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bfr(bfr(__uint_as_float(w[e] << 16) * r) * __uint_as_float(gw[e] << 16));
+      const float hi = bfr(bfr(__uint_as_float(w[e] & 0xFFFF0000u) * r) * __uint_as_float(gw[e] & 0xFFFF0000u));
+      __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+      o[e] = *reinterpret_cast<uint32_t*>(&pr);
+    }
+    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// The packed greedy key of each row of fp32 logits (`cols` of them, vocabulary
+// ids id0 .. id0 + cols - 1 on this rank): float_key(max) << 32 | (2^32 - 1 -
+// id of the first maximum). The largest key over the ranks is the row's
+// greedy id with the lowest index on ties. One CTA of 1024 threads per row.
+__global__ void __launch_bounds__(1024) argmax_keys_kernel(const float* x, int cols, int id0,
+                                                           unsigned long long* keys) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const float* rowf = x + (size_t)blockIdx.x * cols;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < cols; i += 1024) {
+    const float v = __ldg(rowf + i);
+    if (v > best) {
+      best = v;
+      idx = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = idx;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = bv[lane];
+    idx = bi[lane];
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > best || (ov == best && oi < idx)) {
+        best = ov;
+        idx = oi;
+      }
+    }
+    if (lane == 0) {
+      const uint32_t id = (uint32_t)id0 + (uint32_t)(idx == 0x7fffffff ? 0 : idx);
+      keys[blockIdx.x] =
+          ((unsigned long long)float_key(best) << 32) | (unsigned long long)(0xFFFFFFFFu - id);
+    }
+  }
+}
+
+// keys [W][B] (every rank's argmax_keys) -> ids [B]: the largest key of each
+// row, unpacked. One thread per row.
+__global__ void keys_to_ids_kernel(const unsigned long long* keys, int W, int B, int64_t* ids) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  unsigned long long k = keys[b];
+  for (int r = 1; r < W; ++r) k = max(k, keys[(size_t)r * B + b]);
+  ids[b] = (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
 }
 
 }  // namespace mk

@@ -6,15 +6,16 @@
 // One CTA computes a 128-row tile of W against all of X:
 //  * A = the W tile (128 rows; past N the TMA fills zeros), B = X (BP rows:
 //    the batch padded to 16, 32 or 64 with zero rows), both K-major with the
-//    128-byte swizzle, loaded by 2-D
+//    128-byte swizzle (BP = 128 for prompt prefill: 128 token rows), loaded by 2-D
 //    TMA boxes of 64 columns (no multicast) into a ring of kGemmStages stages
 //    with full/empty mbarriers;
 //  * one lane issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32, M = 128,
 //    N = BP, K = 16; four per 64-column stage) into a TMEM accumulator of BP
 //    columns; tcgen05.commit frees each stage and finally signals the
 //    epilogue;
-//  * four warps read the accumulator back (tcgen05.ld.32x32b: warp w owns
-//    TMEM lanes = W rows 32w..32w+31) and write Y[b][n] (coalesced along n);
+//  * four warps read the accumulator back 32 columns at a time
+//    (tcgen05.ld.32x32b: warp w owns TMEM lanes = W rows 32w..32w+31) and
+//    write Y[b][n] (coalesced along n);
 //  * narrow W (16-24 tiles for 148 SMs) is split along K over the CTAs of a
 //    thread-block cluster (at most 8, one cluster per tile): each CTA stages
 //    its fp32 accumulator in its (then idle) ring memory, and after a cluster
@@ -111,10 +112,11 @@ __device__ __forceinline__ constexpr uint32_t gemm_idesc() {
          ((uint32_t)(kGemmTileN >> 4) << 24);
 }
 
-template <int BP>
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[BP]) {
-  uint32_t r[BP];
-  if constexpr (BP == 16) {
+// CB (16 or 32) consecutive fp32 accumulator columns of this thread's TMEM lane.
+template <int CB>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, float (&v)[CB]) {
+  uint32_t r[CB];
+  if constexpr (CB == 16) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
@@ -122,33 +124,30 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[BP]) {
           "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
   } else {
-#pragma unroll
-    for (int c = 0; c < BP; c += 32) {
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-          "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(r[c + 0]), "=r"(r[c + 1]), "=r"(r[c + 2]), "=r"(r[c + 3]), "=r"(r[c + 4]),
-            "=r"(r[c + 5]), "=r"(r[c + 6]), "=r"(r[c + 7]), "=r"(r[c + 8]), "=r"(r[c + 9]),
-            "=r"(r[c + 10]), "=r"(r[c + 11]), "=r"(r[c + 12]), "=r"(r[c + 13]), "=r"(r[c + 14]),
-            "=r"(r[c + 15]), "=r"(r[c + 16]), "=r"(r[c + 17]), "=r"(r[c + 18]), "=r"(r[c + 19]),
-            "=r"(r[c + 20]), "=r"(r[c + 21]), "=r"(r[c + 22]), "=r"(r[c + 23]), "=r"(r[c + 24]),
-            "=r"(r[c + 25]), "=r"(r[c + 26]), "=r"(r[c + 27]), "=r"(r[c + 28]), "=r"(r[c + 29]),
-            "=r"(r[c + 30]), "=r"(r[c + 31])
-          : "r"(taddr + c));
-    }
+    static_assert(CB == 32, "chunks of 16 or 32 columns");
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
   }
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < BP; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < CB; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// One output element: fp32 as is, or + residual and one bf16 rounding.
+// One output element: fp32 as is, or rounded to bf16 and, with a residual,
+// added to it and rounded again (HF's decoder layer: h = bf16(h + bf16(W a))).
 __device__ __forceinline__ void g_store(const GemmParams& p, size_t o, float y) {
   if (p.out_f32) {
     p.out_f32[o] = y;
     return;
   }
-  if (p.residual) y += __bfloat162float(p.residual[o]);
+  if (p.residual) y = __bfloat162float(__float2bfloat16_rn(y)) + __bfloat162float(p.residual[o]);
   p.out[o] = __float2bfloat16_rn(y);
 }
 
@@ -251,15 +250,19 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   // ---- epilogue: warp w reads TMEM lanes 32w..32w+31 = W rows of the tile
   const bool good = g_wait(p, sa(&done), 0, 103) && nk > 0;
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  float v[BP];
-  tmem_ld_cols<BP>(tmem + ((uint32_t)(warp * 32) << 16), v);
+  constexpr int CB = BP < 32 ? BP : 32;  // accumulator columns read per tcgen05.ld
+  const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
   if (p.splits == 1) {
     const int n = tile * kGemmTileN + warp * 32 + lane;
-    if (good && n < p.N) {  // rows past N (the last tile's) were zero-filled by TMA
+    for (int c0 = 0; c0 < BP && c0 < p.B; c0 += CB) {  // warp-uniform: the loads stay aligned
+      float v[CB];
+      tmem_ld_chunk<CB>(tlane + c0, v);
+      if (good && n < p.N) {  // rows past N (the last tile's) were zero-filled by TMA
 #pragma unroll
-      for (int b = 0; b < BP; ++b) {
-        if (b >= p.B) break;
-        g_store(p, (size_t)b * p.N + n, v[b]);
+        for (int b = 0; b < CB; ++b) {
+          if (c0 + b >= p.B) break;
+          g_store(p, (size_t)(c0 + b) * p.N + n, v[b]);
+        }
       }
     }
   } else {
@@ -268,11 +271,15 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
     // the cluster's stages in split order. Both cluster barriers are reached
     // by every thread on every path, so no CTA waits for one that left.
     const int r = warp * 32 + lane;
+    for (int c0 = 0; c0 < BP; c0 += CB) {
+      float v[CB];
+      tmem_ld_chunk<CB>(tlane + c0, v);
 #pragma unroll
-    for (int b = 0; b < BP; ++b)
-      asm volatile("st.shared.f32 [%0], %1;" ::"r"(ring + (uint32_t)(b * kGemmTileN + r) * 4),
-                   "f"(good ? v[b] : 0.f)
-                   : "memory");
+      for (int b = 0; b < CB; ++b)
+        asm volatile("st.shared.f32 [%0], %1;" ::"r"(ring + (uint32_t)((c0 + b) * kGemmTileN + r) * 4),
+                     "f"(good ? v[b] : 0.f)
+                     : "memory");
+    }
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                      : "memory");
     const int E = p.B * kGemmTileN;

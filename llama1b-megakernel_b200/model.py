@@ -55,6 +55,10 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
             self._tokens = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
             self._positions = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
             self._next = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
+            # pinned staging for forward(): token + position in, next id out
+            self._h_in = torch.zeros(2, max_batch, dtype=torch.int32).pin_memory()
+            self._d_in = torch.zeros(2, max_batch, dtype=torch.int32, device=self.device)
+            self._h_next = torch.zeros(max_batch, dtype=torch.int32).pin_memory()
             # lm_head rows this model scores (a tensor-parallel rank scores a slice)
             self.lm_rows = lm_rows or cfg.vocab
             self._logits = torch.empty(max_batch, self.lm_rows, dtype=torch.float32,
@@ -126,11 +130,16 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         return self._trace
 
     def _kv_struct(self, kv: PagedKVCache) -> _lib.MkKVCache:
+        st = kv.__dict__.get("_mk_struct")
+        if st is not None and st[0] is self:
+            return st[1]
         if kv.num_pages > self.kv.num_pages or kv.max_blocks != self.kv.max_blocks \
                 or kv.page_size != self.page_size:
             raise ValueError("cache geometry differs from the one the model was initialised with")
-        return _lib.MkKVCache(k_pages=kv.k_pages.data_ptr(), v_pages=kv.v_pages.data_ptr(),
-                              block_tables=kv.block_tables.data_ptr())
+        s = _lib.MkKVCache(k_pages=kv.k_pages.data_ptr(), v_pages=kv.v_pages.data_ptr(),
+                           block_tables=kv.block_tables.data_ptr())
+        kv._mk_struct = (self, s)  # the pool tensors never move, so the struct stays valid
+        return s
 
     @staticmethod
     def _stream_ptr(stream) -> int:
@@ -172,7 +181,8 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         ``position_ids`` [B, T] default to each sequence's current length.
         K/V rows are written at those positions of ``past_key_values`` (the
         model's own cache when None). Returns the last step's fp32 logits
-        [B, V], its greedy ids [B] and the cache.
+        [B, V] (on the device), its greedy ids [B] int64 (on the host once
+        synchronised; the device tensor with ``sync=False``) and the cache.
         """
         kv = past_key_values if past_key_values is not None else self.kv
         ids = torch.as_tensor(input_ids)
@@ -185,22 +195,33 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
             start = torch.tensor(kv.seq_lens[:B], dtype=torch.int64)
             position_ids = start[:, None] + torch.arange(T)[None, :]
         pos = torch.as_tensor(position_ids).reshape(B, T)
-        pos_host = pos.cpu()
+        pos_host = pos if pos.device.type == "cpu" else pos.cpu()
+        last = pos_host.max(dim=1).values.tolist() if T > 1 else pos_host[:, 0].tolist()
         for b in range(B):
-            kv.reserve(b, int(pos_host[b].max()) + 1)
-        ids_dev = ids.to(device=self.device, dtype=torch.int32, non_blocking=True)
-        pos_dev = pos.to(device=self.device, dtype=torch.int32, non_blocking=True)
+            kv.reserve(b, last[b] + 1)
         logits = self._logits[:B] if return_logits else None
-        for t in range(T):
-            tok = ids_dev[:, t].contiguous()
-            ps = pos_dev[:, t].contiguous()
-            self.launch(tok, ps, kv, logits if t == T - 1 else None, self._next[:B])
+        if T == 1 and sync and ids.device.type == "cpu":
+            # one pinned staging buffer, one H2D copy for token and position
+            # (reused by the next call, so only when this call synchronises)
+            self._h_in[0, :B].copy_(ids[:, 0])
+            self._h_in[1, :B].copy_(pos_host[:, 0])
+            self._d_in[:, :B].copy_(self._h_in[:, :B], non_blocking=True)
+            self.launch(self._d_in[0, :B], self._d_in[1, :B], kv, logits, self._next[:B])
+        else:
+            ids_dev = ids.to(device=self.device, dtype=torch.int32, non_blocking=True)
+            pos_dev = pos.to(device=self.device, dtype=torch.int32, non_blocking=True)
+            for t in range(T):
+                self.launch(ids_dev[:, t].contiguous(), pos_dev[:, t].contiguous(), kv,
+                            logits if t == T - 1 else None, self._next[:B])
         for b in range(B):
-            kv.seq_lens[b] = max(kv.seq_lens[b], int(pos_host[b].max()) + 1)
-        if sync:
-            self.sync()
+            if last[b] + 1 > kv.seq_lens[b]:
+                kv.seq_lens[b] = last[b] + 1
+        if not sync:
+            return DecodeOutput(logits, self._next[:B].to(torch.int64), kv)
+        self._h_next[:B].copy_(self._next[:B], non_blocking=True)
+        self.sync()
         return DecodeOutput(logits.clone() if logits is not None else None,
-                            self._next[:B].to(torch.int64), kv)
+                            self._h_next[:B].to(torch.int64), kv)
 
     def sample(self, logits: torch.Tensor, top_k: int = 1, top_p: float = 1.0,
                temperature: float = 1.0, seed: int = 0, step: int = 0,

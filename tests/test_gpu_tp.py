@@ -63,6 +63,17 @@ def test_tp2_matches_single_gpu(tmp_path, config):
     assert r["ids_match"] >= 0.95, r
     assert r["generate_self_consistent"], r
     assert r["batch_cos_min"] >= 0.9999, r
+    _check_oracle_and_batched(r)
+
+
+def _check_oracle_and_batched(r):
+    # against the oracle: the single-GPU parity bar (these are 2- and 3-layer models)
+    assert r["oracle_cos_min"] >= 0.999 and r["oracle_maxabs_max"] <= 3e-2, r
+    # batched TP step: same bar against the single-GPU batched step and the oracle
+    assert r["tp_batched_cos_min"] >= 0.9999, r
+    assert r["tp_batched_oracle_cos_min"] >= 0.999, r
+    assert r["tp_batched_oracle_maxabs"] <= 3e-2, r
+    assert r["tp_batched_ids_equal"] and r["tp_batched_oracle_ids_equal"], r
 
 
 @pytest.mark.skipif(_gpus() < 8, reason="needs 8 GPUs")
@@ -72,3 +83,4 @@ def test_tp8_one_kv_head_per_gpu(tmp_path):
     assert r["cos_min"] >= 0.9999 and r["maxabs_max"] <= 5e-2, r
     assert r["ids_match"] >= 0.95, r
     assert r["generate_self_consistent"], r
+    _check_oracle_and_batched(r)

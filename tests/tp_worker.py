@@ -14,7 +14,13 @@ tokens and positions:
 * greedy ids, step by step, teacher-forced on the single-GPU tokens;
 * the on-device greedy feedback (``generate``) against the same tokens fed
   through ``forward`` step by step;
-* two sequences of different lengths in one batch.
+* two sequences of different lengths in one batch;
+* per-step logits against the CPU oracle (the reference's PyTorch path
+  restated, oracle/llama_oracle.py) on the single-GPU model's cache;
+* the batched tensor-parallel step (``BatchedDecoder`` on the TP model: the
+  tcgen05 GEMMs on each rank's shard, NCCL all-reduce of the o_proj / down
+  partial sums, vocabulary-parallel lm_head with a gathered argmax) at batch
+  4 against the single-GPU batched step and the oracle.
 
 Rank 0 writes the measurements to ``--out`` as JSON; the test asserts.
 """
@@ -36,6 +42,7 @@ from llama1b_megakernel_b200 import synthetic as syn  # noqa: E402
 from llama1b_megakernel_b200 import tp  # noqa: E402
 from llama1b_megakernel_b200.config import LLAMA_3_2_1B, MID, SMALL  # noqa: E402
 from llama1b_megakernel_b200.model import MegakernelLlamaForCausalLM  # noqa: E402
+from oracle import llama_oracle as O  # noqa: E402
 
 CONFIGS = {"mid": MID, "small": SMALL, "1b": LLAMA_3_2_1B}
 
@@ -60,6 +67,7 @@ def main() -> None:
     res: dict = {"world": world, "config": args.config}
     try:
         w = syn.make_weights(cfg, seed=5, device=dev)
+        w_cpu = {k: v.cpu() for k, v in w.items()} if rank == 0 else None
         m = tp.TensorParallelLlamaForCausalLM(cfg, w, max_batch=2, max_seq_len=256, page_size=32,
                                               device=dev)
         ref = MegakernelLlamaForCausalLM(cfg, w, max_batch=2, max_seq_len=256, page_size=32,
@@ -99,6 +107,26 @@ def main() -> None:
                 maxabs.append(float((o.logits - r.logits).abs().max()))
                 same.append(int(o.next_ids[0]) == int(r.next_ids[0]))
                 t = [int(r.next_ids[0])]
+        # ---- the TP step against the oracle (on the single-GPU model's cache)
+        ocos, omax = [], []
+        for s in range(3):
+            tt = torch.tensor(t, dtype=torch.int64, device=dev)
+            dist.broadcast(tt, 0)
+            p_ = 17 + args.steps + s
+            if rank == 0:
+                ref.kv.reserve(0, p_ + 1)  # the oracle copies the block table
+                kv_o = O.OracleKV(ref.kv.k_pages.cpu().clone(), ref.kv.v_pages.cpu().clone(),
+                                  ref.kv.block_tables.cpu().clone())
+            o = m.forward(tt.cpu().reshape(1, 1), torch.tensor([[p_]]))
+            if rank == 0:
+                want = O.decode_step(cfg, w_cpu, kv_o, [int(tt[0])], [p_])["logits"]
+                r = ref.forward(tt.cpu().reshape(1, 1), torch.tensor([[p_]]))
+                got = o.logits.float().cpu()
+                ocos.append(cos(got, want))
+                omax.append(float((got - want).abs().max()))
+                t = [int(r.next_ids[0])]
+        res["oracle_cos_min"] = min(ocos) if ocos else None
+        res["oracle_maxabs_max"] = max(omax) if omax else None
         res["cos_min"] = min(coss) if coss else None
         res["maxabs_max"] = max(maxabs) if maxabs else None
         res["ids_match"] = sum(same) / len(same) if same else None
@@ -132,6 +160,39 @@ def main() -> None:
             rb = ref.forward(ids, pos, past_key_values=kvr)
             res["batch_cos_min"] = min(cos(ob.logits[b], rb.logits[b]) for b in range(2))
             res["batch_ids_equal"] = bool(torch.equal(ob.next_ids, rb.next_ids))
+        # ---- batched tensor-parallel step (bs 4, ragged cached lengths)
+        from llama1b_megakernel_b200.batched import BatchedDecoder
+
+        B, lens = 4, [37, 64, 5, 100]
+        dec = BatchedDecoder(m, max_batch=B, max_seq_len=128, page_size=32)
+        nkv = lc.num_kv_heads
+        rows = []
+        for b in range(B):
+            k, v = syn.random_kv_rows(cfg, lens[b], seed=31, seq=b, device=dev)
+            rows.append((k, v))
+            dec.kv.fill(b, k[:, g0:g0 + nkv], v[:, g0:g0 + nkv])
+        btok = syn.random_tokens(B, cfg.vocab, seed=33)
+        bpos = torch.tensor(lens, dtype=torch.int32)
+        lg, ids = dec.step(btok, bpos)
+        full = tp.gather_slices(lg.clone(), cfg.vocab, None)
+        ids = ids.cpu()
+        dec.check()
+        if rank == 0:
+            dref = BatchedDecoder(ref, max_batch=B, max_seq_len=128, page_size=32)
+            for b in range(B):
+                dref.kv.fill(b, rows[b][0], rows[b][1])
+            rl, rids = dref.step(btok, bpos)
+            res["tp_batched_cos_min"] = min(cos(full[b], rl[b]) for b in range(B))
+            res["tp_batched_ids_equal"] = bool(torch.equal(ids, rids.cpu()))
+            kv_o = O.OracleKV(dref.kv.k_pages.cpu().clone(), dref.kv.v_pages.cpu().clone(),
+                              dref.kv.block_tables.cpu().clone())
+            want = O.decode_step(cfg, w_cpu, kv_o, btok, lens)["logits"]
+            res["tp_batched_oracle_cos_min"] = min(cos(full[b].cpu(), want[b]) for b in range(B))
+            res["tp_batched_oracle_maxabs"] = float((full.cpu() - want).abs().max())
+            top2 = want.topk(2, dim=-1).values
+            sure = (top2[:, 0] - top2[:, 1]) > 0.05  # rows whose greedy id is not a near-tie
+            res["tp_batched_oracle_ids_equal"] = bool(
+                (ids[sure] == want.argmax(dim=-1)[sure]).all())
         res["ok"] = True
     except Exception as e:  # rank 0 reports; the others' failures surface as timeouts
         res["ok"] = False
