@@ -491,24 +491,30 @@ cudaError_t launch_gemm(const mk::GemmParams& gp, int tiles, int splits, cudaStr
 }  // namespace
 
 namespace {
-// Positions per attention CTA: long enough for every warp to pipeline a few
-// chunks, short enough that batch x kv heads x splits fills the GPU (3 CTAs
-// per SM), a multiple of 128.
+// Positions per attention CTA (a multiple of 32, at least 128 so each of the
+// 4 warps pipelines a chunk or more). The grid is batch x kv heads x splits
+// CTAs over 3 resident CTAs per SM, so the step takes about ceil(CTAs / (3
+// SMs)) waves of one split each: pick the length that minimises waves x
+// (length + the fixed cost of a CTA, ~64 positions' worth), the longer one
+// on ties. (A grid just over one wave, e.g. 512 CTAs of 1,024 positions at
+// bs 64, runs two waves, the second nearly empty.)
 int attn_split_len(int batch, int num_kv_heads, int max_len, int sms) {
-  const long long items = (long long)batch * num_kv_heads;
-  const long long target = 3LL * sms;
-  long long splits = (target + items - 1) / items;
-  if (splits < 1) splits = 1;
-  long long len = (max_len + splits - 1) / splits;
-  len = ((len + 127) / 128) * 128;
-  if (len < 128) len = 128;
-  if (len > 1024) {
-    // At most 1,024 positions a split, cut evenly: 1,088 becomes 2 x 544,
-    // not 1,024 + 64 (CTAs of equal work, measured 7 % faster at bs 64).
-    const long long n = (max_len + 1023) / 1024;
-    len = ((max_len + n - 1) / n + 31) / 32 * 32;
+  const long long pairs = (long long)batch * num_kv_heads;
+  const long long slots = 3LL * sms;
+  const int hi = ((max_len + 31) / 32) * 32;
+  int best = hi;
+  long long best_cost = -1;
+  for (int len = hi; len >= 128; len -= 32) {
+    const long long splits = (max_len + len - 1) / len;
+    const long long waves = (pairs * splits + slots - 1) / slots;
+    const long long cost = waves * (len + 64);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = len;
+    }
+    if (len == 128) break;
   }
-  return (int)len;
+  return best < 128 ? 128 : best;
 }
 int device_sms() {
   int dev = 0, sms = 148;

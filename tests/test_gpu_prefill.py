@@ -104,3 +104,45 @@ def test_generate_with_prefill_agrees_with_kernel_prompt(small):
     b = m.generate(toks, 8, past_key_values=m.new_cache(), prefill=False)
     # the two prompt paths round differently; the first tokens agree
     assert int(a[0, 0]) == int(b[0, 0])
+
+
+def test_llama1b_prefill_128_token_prompt():
+    """BASELINE config 2's prompt: 128 seeded tokens through the prefill
+    kernels of full-size Llama-3.2-1B, against HF on the CPU (the reference's
+    PyTorch path). Every K/V row lands at its position (nothing else in the
+    cache changes), layer-0 rows within a few bf16 ulps, every layer's rows at
+    cosine >= 0.999, and the last position's logits at cosine >= 0.999 with
+    max-abs inside the 1B bf16 envelope (test_gpu_batched.MAXABS_1B)."""
+    from llama1b_megakernel_b200.config import LLAMA_3_2_1B as cfg
+
+    w = syn.make_weights(cfg, seed=0, device="cuda")
+    m = MegakernelLlamaForCausalLM(cfg, w, max_batch=1, max_seq_len=192, page_size=64)
+    w_cpu = {k: v.cpu() for k, v in w.items()}
+    del w
+    toks = syn.random_tokens(128, cfg.vocab, seed=1).reshape(1, -1)
+    m.kv.shuffle_free_pages(3)
+    before_k = m.kv.k_pages.clone()
+    out = m.prefill(toks)
+    hf = O.hf_model(cfg, w_cpu)
+    with torch.no_grad():
+        ref = hf(toks, use_cache=True)
+    rl = ref.logits[0, -1].float()
+    err = float((out.logits[0].cpu() - rl).abs().max())
+    print(f"1B prefill last logits: cos {_cos(out.logits[0].cpu(), rl):.6f} max|diff| {err:.4f}")
+    assert _cos(out.logits[0].cpu(), rl) >= 0.999 and err <= 0.2
+    # rows at exactly positions 0..127 of the sequence's pages, nothing else
+    changed = (m.kv.k_pages != before_k).any(dim=(0, 2, 4))  # [num_pages, page_size]
+    expect = torch.zeros_like(changed)
+    for p in range(128):
+        expect[int(m.kv.block_tables[0, p // 64]), p % 64] = True
+    assert not (changed & ~expect).any(), "prefill wrote outside the prompt's rows"
+    k, v = m.kv.gather(0, 128)
+    for l in range(cfg.num_layers):
+        hk, hv = _hf_kv(ref.past_key_values, l)
+        if l == 0:
+            assert (k[l].float().cpu() - hk.float()).abs().max() <= KV_ROW_TOL
+            assert (v[l].float().cpu() - hv.float()).abs().max() <= KV_ROW_TOL
+        assert _cos(k[l].cpu(), hk) >= 0.999 and _cos(v[l].cpu(), hv) >= 0.999, l
+    assert m.kv.seq_lens[0] == 128
+    del m
+    torch.cuda.empty_cache()
