@@ -333,7 +333,8 @@ def run_ours(args, ws, rank, local):
     sweep = not (args.no_sweep or args.small) and tp_world == 1
     K, W = args.steps, args.warmup
     head_len = CTX + K + W + 2
-    max_seq = max(8192 + 64 if sweep else 0, head_len, PROMPT_LEN + DECODE_STEPS + 2)
+    # (the batched extras run KV length 1024 in caches of 1024 + 64 positions)
+    max_seq = max(8192 + 64 if sweep else 0, head_len, PROMPT_LEN + DECODE_STEPS + 2, CTX + 64)
     w = syn.make_weights(cfg, seed=0, device=dev)
     if tp_world > 1:
         from llama1b_megakernel_b200.tp import TensorParallelLlamaForCausalLM
@@ -557,25 +558,28 @@ def run_tp_batched(model, cfg, dev, ws, B: int = 32, L: int = 1024):
     from llama1b_megakernel_b200.batched import BatchedDecoder
 
     dec = BatchedDecoder(model, max_batch=B, max_seq_len=L + 64, page_size=64)
-    nkv = model.cfg.num_kv_heads
-    g0 = model.tp_rank * nkv
-    for b in range(B):
-        k, v = syn.random_kv_rows(cfg, L, seed=100 + b, seq=b, device=dev)
-        dec.kv.fill(b, k[:, g0:g0 + nkv], v[:, g0:g0 + nkv])
-        del k, v
-    dec.step(syn.random_tokens(B, cfg.vocab, seed=B), torch.full((B,), L, dtype=torch.int32))
-    for _ in range(3):
-        dec.replay(B)
-    torch.cuda.synchronize()
-    barrier(ws)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(21)]
-    ev[0].record()
-    for j in range(20):
-        dec.replay(B)
-        ev[j + 1].record()
-    torch.cuda.synchronize()
-    dec.check()
-    med = max_over_ranks(statistics.median(ev[j].elapsed_time(ev[j + 1]) for j in range(20)), ws)
+    try:
+        nkv = model.cfg.num_kv_heads
+        g0 = model.tp_rank * nkv
+        for b in range(B):
+            k, v = syn.random_kv_rows(cfg, L, seed=100 + b, seq=b, device=dev)
+            dec.kv.fill(b, k[:, g0:g0 + nkv], v[:, g0:g0 + nkv])
+            del k, v
+        dec.step(syn.random_tokens(B, cfg.vocab, seed=B), torch.full((B,), L, dtype=torch.int32))
+        for _ in range(3):
+            dec.replay(B)
+        torch.cuda.synchronize()
+        barrier(ws)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(21)]
+        ev[0].record()
+        for j in range(20):
+            dec.replay(B)
+            ev[j + 1].record()
+        torch.cuda.synchronize()
+        dec.check()
+        med = max_over_ranks(statistics.median(ev[j].elapsed_time(ev[j + 1]) for j in range(20)), ws)
+    finally:
+        dec.close()  # its graphs hold NCCL calls: released before the group is destroyed
     del dec
     torch.cuda.empty_cache()
     return {"batch": B, "kv_len": L, "ms_p50": med, "tok_s": B * 1e3 / med,

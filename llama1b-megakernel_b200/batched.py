@@ -250,6 +250,13 @@ class BatchedDecoder:
         (benchmark loop; no host work)."""
         self._graphs[B][0].replay()
 
+    def close(self) -> None:
+        """Release the captured step graphs. A tensor-parallel rank's graphs hold
+        NCCL collectives, and a process group destroyed while such a graph is
+        alive never finishes tearing down: close the decoder first."""
+        torch.cuda.synchronize(self.dev)
+        self._graphs.clear()
+
     def check(self) -> None:
         torch.cuda.synchronize(self.dev)
         code = int(self.err[0])

@@ -64,6 +64,10 @@ def main() -> None:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
+
+    def stage(what: str) -> None:  # progress on stderr, so a stuck run shows where it stopped
+        print(f"[rank {rank}] {what}", file=sys.stderr, flush=True)
+
     res: dict = {"world": world, "config": args.config}
     try:
         w = syn.make_weights(cfg, seed=5, device=dev)
@@ -76,6 +80,7 @@ def main() -> None:
         lc = tp.shard_config(cfg, world)
         g0 = rank * lc.num_kv_heads
 
+        stage("models built")
         # ---- prompt, then teacher-forced single steps
         prompt = syn.random_tokens(17, cfg.vocab, seed=9).reshape(1, -1)
         out = m.forward(prompt)
@@ -107,8 +112,25 @@ def main() -> None:
                 maxabs.append(float((o.logits - r.logits).abs().max()))
                 same.append(int(o.next_ids[0]) == int(r.next_ids[0]))
                 t = [int(r.next_ids[0])]
-        # ---- the TP step against the oracle (on the single-GPU model's cache)
-        ocos, omax = [], []
+        stage("teacher-forced steps")
+        # ---- the TP step against the oracle (on the single-GPU model's cache).
+        # Configs with Llama-3.2-1B-shaped layers are also evaluated in fp32:
+        # there the bf16 rounding order alone moves logits ~3e-2 or more, so
+        # the bar is the single-GPU test's envelope (distance to fp32 at most
+        # 1.5x the oracle's own, plus 1e-3) rather than a fixed max-abs.
+        w32 = ({k: v.float() for k, v in w_cpu.items()} if rank == 0 and cfg.hidden >= 2048
+               else None)
+
+        def envelope(got, want, kv_o, toks, poss):
+            if w32 is None:
+                return None
+            kv32 = O.OracleKV(kv_o.k_pages.float(), kv_o.v_pages.float(), kv_o.block_tables)
+            truth = O.decode_step(cfg, w32, kv32, toks, poss)["logits"]
+            d_ref = (want - truth).abs().max(dim=-1).values
+            d_got = (got - truth).abs().max(dim=-1).values
+            return float((d_got - 1.5 * d_ref).max())
+
+        ocos, omax, oenv = [], [], []
         for s in range(3):
             tt = torch.tensor(t, dtype=torch.int64, device=dev)
             dist.broadcast(tt, 0)
@@ -124,13 +146,16 @@ def main() -> None:
                 got = o.logits.float().cpu()
                 ocos.append(cos(got, want))
                 omax.append(float((got - want).abs().max()))
+                oenv.append(envelope(got.reshape(1, -1), want.reshape(1, -1), kv_o, [int(tt[0])], [p_]))
                 t = [int(r.next_ids[0])]
         res["oracle_cos_min"] = min(ocos) if ocos else None
         res["oracle_maxabs_max"] = max(omax) if omax else None
+        res["oracle_envelope_excess"] = max(oenv) if oenv and oenv[0] is not None else None
         res["cos_min"] = min(coss) if coss else None
         res["maxabs_max"] = max(maxabs) if maxabs else None
         res["ids_match"] = sum(same) / len(same) if same else None
 
+        stage("oracle steps")
         # ---- free-running greedy generation on device (argmax fed back in the
         # kernel) against the same tokens fed through forward one by one
         p2 = syn.random_tokens(9, cfg.vocab, seed=11).reshape(1, -1)
@@ -160,6 +185,7 @@ def main() -> None:
             rb = ref.forward(ids, pos, past_key_values=kvr)
             res["batch_cos_min"] = min(cos(ob.logits[b], rb.logits[b]) for b in range(2))
             res["batch_ids_equal"] = bool(torch.equal(ob.next_ids, rb.next_ids))
+        stage("generate and ragged batch")
         # ---- batched tensor-parallel step (bs 4, ragged cached lengths)
         from llama1b_megakernel_b200.batched import BatchedDecoder
 
@@ -177,11 +203,13 @@ def main() -> None:
         full = tp.gather_slices(lg.clone(), cfg.vocab, None)
         ids = ids.cpu()
         dec.check()
+        dec.close()  # its graph holds NCCL calls: released before the group is destroyed
         if rank == 0:
             dref = BatchedDecoder(ref, max_batch=B, max_seq_len=128, page_size=32)
             for b in range(B):
                 dref.kv.fill(b, rows[b][0], rows[b][1])
             rl, rids = dref.step(btok, bpos)
+            dref.close()
             res["tp_batched_cos_min"] = min(cos(full[b], rl[b]) for b in range(B))
             res["tp_batched_ids_equal"] = bool(torch.equal(ids, rids.cpu()))
             kv_o = O.OracleKV(dref.kv.k_pages.cpu().clone(), dref.kv.v_pages.cpu().clone(),
@@ -189,10 +217,12 @@ def main() -> None:
             want = O.decode_step(cfg, w_cpu, kv_o, btok, lens)["logits"]
             res["tp_batched_oracle_cos_min"] = min(cos(full[b].cpu(), want[b]) for b in range(B))
             res["tp_batched_oracle_maxabs"] = float((full.cpu() - want).abs().max())
+            res["tp_batched_envelope_excess"] = envelope(full.cpu().float(), want, kv_o, btok, lens)
             top2 = want.topk(2, dim=-1).values
             sure = (top2[:, 0] - top2[:, 1]) > 0.05  # rows whose greedy id is not a near-tie
             res["tp_batched_oracle_ids_equal"] = bool(
                 (ids[sure] == want.argmax(dim=-1)[sure]).all())
+        stage("batched step")
         res["ok"] = True
     except Exception as e:  # rank 0 reports; the others' failures surface as timeouts
         res["ok"] = False
@@ -200,7 +230,10 @@ def main() -> None:
         print(res["error"], flush=True)
     if rank == 0:
         Path(args.out).write_text(json.dumps(res))
+    stage("result written")
+    dist.barrier()
     dist.destroy_process_group()
+    stage("process group destroyed")
 
 
 if __name__ == "__main__":
