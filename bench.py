@@ -584,7 +584,9 @@ def run_tp_batched(model, cfg, dev, ws, B: int = 32, L: int = 1024):
     torch.cuda.empty_cache()
     return {"batch": B, "kv_len": L, "ms_p50": med, "tok_s": B * 1e3 / med,
             "gemm": "mk_gemm_bf16 (tcgen05) on each rank's shard",
-            "collective": "NCCL all-reduce (fp32 partial sums) x 2 per layer inside the CUDA graph"}
+            "collective": "fp32 partial sums read from peer memory over NVLink and summed in rank "
+                          "order inside the add+RMSNorm kernel (mk_allreduce_add_rmsnorm), x 2 per "
+                          "layer; NCCL all-gather of the argmax keys once per step"}
 
 
 def run_case_gemm():

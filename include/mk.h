@@ -348,6 +348,48 @@ int mk_tp_setup(MkModel* m, int32_t rank, int32_t world, int32_t lm_row0, int32_
  * process drives all GPUs (peer access is enabled); exactly one non-NULL. */
 int mk_tp_connect(MkModel* m, const MkIpcHandle* handles, void* const* buffers);
 
+/* ---- Batched tensor-parallel step: the residual all-reduce over peer memory
+ *
+ * Replaces the all-reduce after the row-parallel o_proj and down of the
+ * reference's tensor-parallel decoder (RowParallelLinear, llama.py:437-470)
+ * together with the residual add and RMSNorm that follow it (llama.py:1039-1139)
+ * in ONE kernel per exchange, with no NCCL on the data path. Each rank owns an
+ * exchange buffer of mk_xbuf_bytes(rows, hidden) bytes: two slots of
+ * [rows][hidden] fp32 partial sums (slot e % 2 for exchange e of a step, at
+ * byte offset (e % 2) * rows * hidden * 4) and a block of flag words.
+ * mk_xbuf_alloc allocates and zeroes it on the current device and exports its
+ * IPC handle; mk_xbuf_open maps another rank's buffer on the current device
+ * (peer access enabled on first use); mk_xbuf_close / mk_xbuf_free undo them
+ * (close every mapping on every rank before any owner frees its buffer).
+ *
+ * mk_step_epoch advances the step counter `epoch` (one device word shared by
+ * all exchanges of a step, identical on every rank); launch it once at the
+ * start of every step, before the step's first exchange.
+ *
+ * mk_allreduce_add_rmsnorm, exchange e of the step (0 <= e < 64, each value
+ * once per step, the same sequence on every rank): this rank's partial sums
+ * for the first `rows` rows must already be in its own slot e % 2 (for
+ * instance the fp32 output of mk_gemm_bf16 written there earlier on `stream`).
+ * The kernel posts this rank's tag on every rank's flag word, waits (bounded
+ * by timeout_ns, 0 = 2 s; on expiry error[0] = 3 and the rows are left
+ * unchanged) for every rank's tag, reads the `world` partials of its rows from
+ * the owners' buffers over NVLink (plain loads), sums them in rank order (so
+ * every rank computes the same bits) and then, as mk_add_rmsnorm_rows,
+ * x = bf16(x + bf16(sum)) in place and out = RMSNorm(x) * gamma. `peers` is a
+ * device array of `world` buffer addresses as mapped on this GPU (the rank's
+ * own at index `rank`); `rows_cap` the rows the buffers were sized for.
+ * Asynchronous on `stream`. */
+int64_t mk_xbuf_bytes(int32_t rows, int32_t hidden);
+int mk_xbuf_alloc(int64_t bytes, MkIpcHandle* handle, void** ptr);
+int mk_xbuf_open(const MkIpcHandle* handle, void** ptr);
+int mk_xbuf_close(void* ptr);
+int mk_xbuf_free(void* ptr);
+int mk_step_epoch(uint32_t* epoch, void* stream);
+int mk_allreduce_add_rmsnorm(const uint64_t* peers, int32_t rank, int32_t world, int32_t rows_cap,
+                             int32_t exchange, const uint32_t* epoch, void* x, const void* gamma,
+                             float eps, int32_t rows, int32_t hidden, void* out, int32_t* error,
+                             uint64_t timeout_ns, void* stream);
+
 /* The largest number of ring fills a consumer warp goes between two waits in
  * the kernel's schedule for this geometry, batch and grid (-1 if a warp's
  * first wait comes at fill 64 or later). mk_init refuses a geometry whose gap

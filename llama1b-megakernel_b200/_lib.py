@@ -26,7 +26,9 @@ EXPORTED = (
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_schedule_gap", "mk_sample", "mk_paged_attention_workspace",
     "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_argmax_rows",
-    "mk_add_rmsnorm_rows", "mk_argmax_keys", "mk_keys_to_ids", "mk_tp_setup", "mk_tp_connect", "mk_last_error",
+    "mk_add_rmsnorm_rows", "mk_argmax_keys", "mk_keys_to_ids", "mk_tp_setup", "mk_tp_connect",
+    "mk_xbuf_bytes", "mk_xbuf_alloc", "mk_xbuf_open", "mk_xbuf_close", "mk_xbuf_free", "mk_step_epoch",
+    "mk_allreduce_add_rmsnorm", "mk_last_error",
     "mk_destroy",
 )
 
@@ -116,11 +118,21 @@ def load() -> ctypes.CDLL:
     lib.mk_keys_to_ids.argtypes = [VP, I32, I32, VP, VP]
     lib.mk_tp_setup.argtypes = [VP, I32, I32, I32, I32, P(MkIpcHandle), P(VP)]
     lib.mk_tp_connect.argtypes = [VP, P(MkIpcHandle), P(VP)]
+    lib.mk_xbuf_bytes.argtypes = [I32, I32]
+    lib.mk_xbuf_bytes.restype = ctypes.c_int64
+    lib.mk_xbuf_alloc.argtypes = [ctypes.c_int64, P(MkIpcHandle), P(VP)]
+    lib.mk_xbuf_open.argtypes = [P(MkIpcHandle), P(VP)]
+    lib.mk_xbuf_close.argtypes = [VP]
+    lib.mk_xbuf_free.argtypes = [VP]
+    lib.mk_step_epoch.argtypes = [VP, VP]
+    lib.mk_allreduce_add_rmsnorm.argtypes = [VP, I32, I32, I32, I32, VP, VP, VP, ctypes.c_float,
+                                             I32, I32, VP, VP, ctypes.c_uint64, VP]
     lib.mk_last_error.argtypes = []
     lib.mk_last_error.restype = ctypes.c_char_p
     lib.mk_destroy.argtypes = [VP]
     for name in EXPORTED:
-        if name not in ("mk_last_error", "mk_paged_attention_workspace", "mk_gemm_workspace"):
+        if name not in ("mk_last_error", "mk_paged_attention_workspace", "mk_gemm_workspace",
+                        "mk_xbuf_bytes"):
             getattr(lib, name).restype = ctypes.c_int
     _lib = lib
     return lib

@@ -24,10 +24,13 @@ path runs one step as:
 Tensor parallelism (``model`` a ``TensorParallelLlamaForCausalLM``; BASELINE
 config 5 at bs 32): each rank holds its q / kv heads, MLP rows and lm_head
 rows (tp.py). The q/k/v and gate/up GEMMs, RoPE, the KV cache and attention
-are local; o_proj and down produce fp32 partial sums over the rank's input
-columns (RowParallelLinear, llama.py:437-470), which an NCCL all-reduce sums
-inside the captured graph, and ``mk_add_rmsnorm_rows`` adds the sum to the
-residual and normalises for the next GEMM. The lm_head scores the rank's
+are local; o_proj and down write fp32 partial sums over the rank's input
+columns (RowParallelLinear, llama.py:437-470) into the rank's exchange buffer,
+and one kernel per exchange (``mk_allreduce_add_rmsnorm``) reads every rank's
+partial over NVLink from peer memory, sums them in rank order, adds the sum to
+the residual and normalises for the next GEMM: no NCCL on that path. The
+buffers are mapped on every GPU through CUDA IPC handles exchanged once over
+the group at construction. The lm_head scores the rank's
 vocabulary rows; ``mk_argmax_keys`` packs each row's maximum and global id
 into one integer key, the keys are all-gathered and ``mk_keys_to_ids`` takes
 the largest (lowest id on ties).
@@ -79,6 +82,41 @@ class BatchedDecoder:
         self.gwork = torch.zeros(max(gws, 16), dtype=torch.uint8, device=self.dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self._graphs: dict[int, tuple] = {}
+        self._xbuf = None
+        if self.tp_world > 1:
+            self._open_exchange()
+
+    def _open_exchange(self) -> None:
+        """This rank's exchange buffer (two fp32 [max_batch][hidden] slots and the
+        flag words) and every other rank's, mapped on this GPU."""
+        from . import tp
+
+        lib, H = self.lib, self.cfg.hidden
+        torch.cuda.set_device(self.dev)
+        nbytes = lib.mk_xbuf_bytes(self.max_batch, H)
+        handle, own = _lib.MkIpcHandle(), ctypes.c_void_p()
+        _lib.check(lib.mk_xbuf_alloc(nbytes, ctypes.byref(handle), ctypes.byref(own)))
+        self._xbuf = own.value
+        self._xpeer_open: list[int] = []
+        handles = tp.exchange_handles(bytes(handle.bytes), self.group)
+        rank = dist.get_rank(self.group)
+        addrs = []
+        for r, hb in enumerate(handles):
+            if r == rank:
+                addrs.append(self._xbuf)
+                continue
+            h, ptr = _lib.MkIpcHandle(), ctypes.c_void_p()
+            ctypes.memmove(h.bytes, hb, 64)
+            _lib.check(lib.mk_xbuf_open(ctypes.byref(h), ctypes.byref(ptr)))
+            self._xpeer_open.append(ptr.value)
+            addrs.append(ptr.value)
+        self.tp_rank = rank
+        self.xpeers = torch.tensor(addrs, dtype=torch.int64, device=self.dev)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
+
+    def _xslot(self, e: int) -> int:
+        """Device address of this rank's partial-sum slot for exchange e."""
+        return self._xbuf + (e % 2) * self.max_batch * self.cfg.hidden * 4
 
     # ------------------------------------------------------------------ step
     def _attention(self, q, layer, lengths, B, out):
@@ -92,13 +130,16 @@ class BatchedDecoder:
 
     def _gemm(self, w, x, rows, out=None, out_f32=None, residual=None):
         """Y = X W^T (+ residual) on the tensor cores (``mk_gemm_bf16``); X has
-        the padded row count, its first ``rows`` rows real."""
+        the padded row count, its first ``rows`` rows real. ``out_f32`` is a
+        tensor or a device address."""
         n, k = w.shape
+        if isinstance(out_f32, torch.Tensor):
+            out_f32 = out_f32.data_ptr()
         _lib.check(self.lib.mk_gemm_bf16(
             w.data_ptr(), n, k, x.data_ptr(), rows, x.shape[0],
             residual.data_ptr() if residual is not None else None,
             out.data_ptr() if out is not None else None,
-            out_f32.data_ptr() if out_f32 is not None else None,
+            out_f32,
             self.gwork.data_ptr(), self.gwork.numel(), self.err.data_ptr(),
             torch.cuda.current_stream().cuda_stream))
 
@@ -111,7 +152,6 @@ class BatchedDecoder:
                    attn=z(BP, c.num_q_heads * 64), act=z(BP, c.intermediate),
                    qkv=z(B, nh * 64), gu=z(B, 2 * c.intermediate))
         if self.tp_world > 1:
-            buf["part"] = torch.zeros(B, c.hidden, dtype=torch.float32, device=dev)
             buf["keys"] = torch.zeros(B, dtype=torch.int64, device=dev)
             buf["keys_all"] = torch.zeros(self.tp_world * B, dtype=torch.int64, device=dev)
         return buf
@@ -156,10 +196,18 @@ class BatchedDecoder:
         H, NQ, NKV, I, L = c.hidden, c.num_q_heads, c.num_kv_heads, c.intermediate, c.num_layers
         st = torch.cuda.current_stream().cuda_stream
         x, h, q, attn, act, qkv, gu = (buf[k] for k in ("x", "h", "q", "attn", "act", "qkv", "gu"))
-        part, keys, keys_all = buf["part"], buf["keys"], buf["keys_all"]
+        keys, keys_all = buf["keys"], buf["keys_all"]
         x.copy_(pw.embed[tokens.long()])
         lengths = (positions + 1).to(torch.int32)
         eps = ctypes.c_float(c.rms_eps)
+        _lib.check(lib.mk_step_epoch(self.epoch.data_ptr(), st))
+
+        def exchange(e: int, gamma) -> None:  # x += sum of the ranks' partials; h = norm(x)
+            _lib.check(lib.mk_allreduce_add_rmsnorm(
+                self.xpeers.data_ptr(), self.tp_rank, self.tp_world, self.max_batch, e,
+                self.epoch.data_ptr(), x.data_ptr(), gamma.data_ptr(), eps, B, H, h.data_ptr(),
+                self.err.data_ptr(), 0, st))
+
         _lib.check(lib.mk_rmsnorm_rows(x.data_ptr(), pw.norm_attn[0].data_ptr(), eps, B, H,
                                        h.data_ptr(), st))
         for l in range(L):
@@ -170,18 +218,12 @@ class BatchedDecoder:
                 kv.page_size, NQ, NKV, B, q.data_ptr(), kv.k_pages[l].data_ptr(),
                 kv.v_pages[l].data_ptr(), self.err.data_ptr(), st))
             self._attention(q, l, lengths, B, attn)
-            self._gemm(pw.w_o[l], attn, B, out_f32=part)  # this rank's partial o_proj
-            dist.all_reduce(part, group=self.group)
-            _lib.check(lib.mk_add_rmsnorm_rows(x.data_ptr(), part.data_ptr(),
-                                               pw.norm_mlp[l].data_ptr(), eps, B, H,
-                                               h.data_ptr(), st))
+            self._gemm(pw.w_o[l], attn, B, out_f32=self._xslot(2 * l))  # partial o_proj
+            exchange(2 * l, pw.norm_mlp[l])
             self._gemm(pw.w_gate_up[l].view(2 * I, H), h, B, out=gu)
             _lib.check(lib.mk_swiglu(gu.data_ptr(), B * I, act.data_ptr(), st))
-            self._gemm(pw.w_down[l], act, B, out_f32=part)  # this rank's partial down
-            dist.all_reduce(part, group=self.group)
-            gamma = pw.norm_attn[l + 1] if l + 1 < L else pw.norm_final
-            _lib.check(lib.mk_add_rmsnorm_rows(x.data_ptr(), part.data_ptr(), gamma.data_ptr(),
-                                               eps, B, H, h.data_ptr(), st))
+            self._gemm(pw.w_down[l], act, B, out_f32=self._xslot(2 * l + 1))  # partial down
+            exchange(2 * l + 1, pw.norm_attn[l + 1] if l + 1 < L else pw.norm_final)
         row0, rows = m.lm_row0, m.lm_rows
         self._gemm(pw.embed[row0:row0 + rows], h, B, out_f32=logits_out)
         _lib.check(lib.mk_argmax_keys(logits_out.data_ptr(), B, rows, row0, keys.data_ptr(), st))
@@ -251,11 +293,21 @@ class BatchedDecoder:
         self._graphs[B][0].replay()
 
     def close(self) -> None:
-        """Release the captured step graphs. A tensor-parallel rank's graphs hold
-        NCCL collectives, and a process group destroyed while such a graph is
-        alive never finishes tearing down: close the decoder first."""
+        """Release the captured step graphs and, on a tensor-parallel rank, the
+        exchange buffers (every rank unmaps the others' buffers before any frees
+        its own). A rank's graphs hold an NCCL collective (the argmax keys), and
+        a process group destroyed while such a graph is alive never finishes
+        tearing down: close the decoder first (on every rank of the group)."""
         torch.cuda.synchronize(self.dev)
         self._graphs.clear()
+        if self._xbuf is not None:
+            dist.barrier(group=self.group)  # no rank reads a peer's buffer any more
+            for ptr in self._xpeer_open:
+                _lib.check(self.lib.mk_xbuf_close(ptr))
+            self._xpeer_open = []
+            dist.barrier(group=self.group)  # every mapping of every buffer is gone
+            _lib.check(self.lib.mk_xbuf_free(self._xbuf))
+            self._xbuf = None
 
     def check(self) -> None:
         torch.cuda.synchronize(self.dev)
@@ -263,5 +315,6 @@ class BatchedDecoder:
         if code:
             self.err.zero_()
             what = ("a block table names a page outside the pool" if code == 1 else
+                    "a tensor-parallel exchange waited too long for another rank" if code == 3 else
                     f"a tcgen05 GEMM wait ran out (code {code})")
             raise _lib.MkError(_lib.MK_EDEVICE, f"batched step: {what}")

@@ -1035,6 +1035,88 @@ int mk_add_rmsnorm_rows(void* x, const float* sum, const void* gamma, float eps,
   return MK_OK;
 }
 
+int64_t mk_xbuf_bytes(int32_t rows, int32_t hidden) {
+  if (rows < 1 || hidden < 8 || hidden % 8) return 0;
+  return (int64_t)mk::xchg_bytes(rows, hidden);
+}
+
+int mk_xbuf_alloc(int64_t bytes, MkIpcHandle* handle, void** ptr) {
+  if (!handle || !ptr || bytes < 1) return fail(MK_EINVAL, "handle, ptr and bytes >= 1 are required");
+  *ptr = nullptr;
+  void* buf = nullptr;
+  MK_CUDA(cudaMalloc(&buf, (size_t)bytes));
+  cudaError_t e = cudaMemset(buf, 0, (size_t)bytes);  // flag 0 is below every tag
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, buf);
+  if (e != cudaSuccess) {
+    cudaFree(buf);
+    return fail(MK_ECUDA, "exchange buffer: %s", cudaGetErrorString(e));
+  }
+  memcpy(handle, &h, sizeof(h));
+  *ptr = buf;
+  return MK_OK;
+}
+
+int mk_xbuf_open(const MkIpcHandle* handle, void** ptr) {
+  if (!handle || !ptr) return fail(MK_EINVAL, "handle and ptr are required");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  MK_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MK_OK;
+}
+
+int mk_xbuf_close(void* ptr) {
+  if (!ptr) return MK_OK;
+  MK_CUDA(cudaIpcCloseMemHandle(ptr));
+  return MK_OK;
+}
+
+int mk_xbuf_free(void* ptr) {
+  if (!ptr) return MK_OK;
+  MK_CUDA(cudaFree(ptr));
+  return MK_OK;
+}
+
+int mk_step_epoch(uint32_t* epoch, void* stream) {
+  if (!epoch) return fail(MK_EINVAL, "epoch is NULL");
+  MK_CUDA(launch_pdl(mk::epoch_advance_kernel, dim3(1), dim3(32), 0,
+                     static_cast<cudaStream_t>(stream), epoch));
+  return MK_OK;
+}
+
+int mk_allreduce_add_rmsnorm(const uint64_t* peers, int32_t rank, int32_t world, int32_t rows_cap,
+                             int32_t exchange, const uint32_t* epoch, void* x, const void* gamma,
+                             float eps, int32_t rows, int32_t hidden, void* out, int32_t* error,
+                             uint64_t timeout_ns, void* stream) {
+  if (!peers || !epoch || !x || !gamma || !out || !error) return fail(MK_EINVAL, "NULL argument");
+  if (world < 2 || world > mk::kMaxTp || rank < 0 || rank >= world)
+    return fail(MK_EINVAL, "rank %d of world %d (2 .. %d GPUs)", rank, world, mk::kMaxTp);
+  if (rows < 1 || rows > rows_cap || hidden < 8 || hidden % 8)
+    return fail(MK_EINVAL, "rows %d (buffer rows %d), hidden %d", rows, rows_cap, hidden);
+  if (exchange < 0 || exchange >= mk::kXchgPerStep)
+    return fail(MK_EINVAL, "exchange %d outside [0, %d)", exchange, mk::kXchgPerStep);
+  if (!aligned16(x) || !aligned16(gamma) || !aligned16(out)) return fail(MK_EINVAL, "16-byte alignment");
+  mk::XchgParams xp{};
+  xp.peers = reinterpret_cast<const unsigned long long*>(peers);
+  xp.rank = rank;
+  xp.W = world;
+  xp.rows = rows_cap;
+  xp.H = hidden;
+  xp.exchange = exchange;
+  xp.epoch = epoch;
+  xp.x = static_cast<mk::bf16*>(x);
+  xp.gamma = static_cast<const mk::bf16*>(gamma);
+  xp.eps = eps;
+  xp.y = static_cast<mk::bf16*>(out);
+  xp.error = error;
+  xp.timeout_ns = timeout_ns ? timeout_ns : 2000000000ull;
+  MK_CUDA(launch_pdl(mk::xreduce_add_rmsnorm_kernel, dim3(rows), dim3(256), 0,
+                     static_cast<cudaStream_t>(stream), xp));
+  return MK_OK;
+}
+
 int mk_argmax_keys(const float* x, int32_t rows, int32_t cols, int32_t id0, uint64_t* keys,
                    void* stream) {
   if (!x || !keys || rows < 1 || cols < 1 || id0 < 0)

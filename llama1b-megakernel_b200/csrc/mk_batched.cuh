@@ -245,6 +245,144 @@ __global__ void __launch_bounds__(256) add_rmsnorm_rows_kernel(__nv_bfloat16* x,
   }
 }
 
+// ---------------------------------------------------------------- peer exchange
+//
+// Tensor parallelism of the batched step without NCCL on the data path. Every
+// rank owns one exchange buffer (plain device memory, mapped on the other
+// GPUs through CUDA IPC): two partial-sum slots of [rows][H] fp32 and a block
+// of 64-bit flag words [2][kMaxTp], flag (slot, src) written by rank src.
+// Exchange e of a step uses slot e % 2: the rank's o_proj or down GEMM writes
+// its fp32 partial into its own slot, then xreduce_add_rmsnorm_kernel posts a
+// tag on every rank's flag (slot, rank), waits (bounded) until every rank's
+// flag in its own buffer carries the tag, and reads the W partials of its rows
+// straight from the owners' memory over NVLink (plain loads, no multicast).
+// Tags grow by step (an epoch word advanced once per step) and exchange, so a
+// flag left by an earlier exchange never passes. Two slots suffice: a rank
+// writes slot e % 2 again only at exchange e + 2, after its exchange e + 1,
+// which waited for every rank's flag e + 1, posted after that rank had
+// finished reading exchange e.
+constexpr int kXchgSlots = 2;
+constexpr int kXchgPerStep = 64;  // exchanges per step at most (2 per decoder layer)
+
+__host__ __device__ inline size_t xchg_slot_floats(int rows, int H) { return (size_t)rows * H; }
+__host__ __device__ inline size_t xchg_flags_offset(int rows, int H) {  // bytes
+  return ((size_t)kXchgSlots * xchg_slot_floats(rows, H) * 4 + 255) & ~(size_t)255;
+}
+__host__ __device__ inline size_t xchg_bytes(int rows, int H) {
+  return xchg_flags_offset(rows, H) + (size_t)kXchgSlots * kMaxTp * 8;
+}
+
+struct XchgParams {
+  const unsigned long long* peers;  // [W] every rank's buffer as mapped here (peers[rank] = own)
+  int rank, W, rows, H, exchange;
+  const uint32_t* epoch;            // the step's epoch (mk_step_epoch)
+  __nv_bfloat16* x;                 // [B][H] residual, updated in place
+  const __nv_bfloat16* gamma;
+  float eps;
+  __nv_bfloat16* y;                 // [B][H] RMSNorm output
+  int* error;
+  unsigned long long timeout_ns;
+};
+
+__global__ void epoch_advance_kernel(uint32_t* epoch) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) epoch[0] += 1u;
+}
+
+// Sum of every rank's partial for this exchange (rank order, the same on every
+// rank), then the add + RMSNorm of add_rmsnorm_rows_kernel. One CTA of 256
+// threads per row.
+__global__ void __launch_bounds__(256) xreduce_add_rmsnorm_kernel(const __grid_constant__ XchgParams p) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[8];
+  __shared__ int bad;
+  const int b = blockIdx.x, tid = threadIdx.x, H = p.H, W = p.W;
+  const int slot = p.exchange % kXchgSlots;
+  const unsigned long long tag =
+      (unsigned long long)p.epoch[0] * kXchgPerStep + (unsigned long long)p.exchange + 1ull;
+  const size_t foff = xchg_flags_offset(p.rows, H) / 8 + (size_t)slot * kMaxTp;  // in u64 words
+  if (tid == 0) bad = 0;
+  // Block 0 posts this rank's flag on every rank (the GEMM that wrote the
+  // partial finished before this grid started).
+  if (b == 0 && tid < W) {
+    __threadfence_system();
+    unsigned long long* f = reinterpret_cast<unsigned long long*>(p.peers[tid]) + foff + p.rank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(tag) : "memory");
+  }
+  if (tid < W) {
+    const unsigned long long* f = reinterpret_cast<const unsigned long long*>(p.peers[p.rank]) + foff + tid;
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+      if (v >= tag) break;
+      if ((it & 63) == 63) {
+        uint64_t now;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+        if (!t0) {
+          t0 = now;
+        } else if (now - t0 > p.timeout_ns) {
+          atomicCAS(p.error, 0, 3);
+          bad = 1;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (bad) return;
+  uint4* xr = reinterpret_cast<uint4*>(p.x + (size_t)b * H);
+  float ss = 0.f;
+  for (int i = tid; i < H / 8; i += 256) {
+    float sv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < W; ++r) {
+      const float4* src = reinterpret_cast<const float4*>(
+          reinterpret_cast<const float*>(p.peers[r]) + (size_t)slot * xchg_slot_floats(p.rows, H) +
+          (size_t)b * H) + 2 * i;
+      const float4 s0 = __ldcv(src), s1 = __ldcv(src + 1);
+      sv[0] += s0.x; sv[1] += s0.y; sv[2] += s0.z; sv[3] += s0.w;
+      sv[4] += s1.x; sv[5] += s1.y; sv[6] += s1.z; sv[7] += s1.w;
+    }
+    const uint4 u = xr[i];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bfr(__uint_as_float(w[e] << 16) + bfr(sv[2 * e]));
+      const float hi = bfr(__uint_as_float(w[e] & 0xFFFF0000u) + bfr(sv[2 * e + 1]));
+      ss = fmaf(lo, lo, ss);
+      ss = fmaf(hi, hi, ss);
+      __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+      o[e] = *reinterpret_cast<uint32_t*>(&pr);
+    }
+    xr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w];
+  const float rn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), p.eps)));
+  const uint4* gr = reinterpret_cast<const uint4*>(p.gamma);
+  uint4* yr = reinterpret_cast<uint4*>(p.y + (size_t)b * H);
+  for (int i = tid; i < H / 8; i += 256) {
+    const uint4 u = xr[i], g = gr[i];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w}, gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = bfr(bfr(__uint_as_float(w[e] << 16) * rn) * __uint_as_float(gw[e] << 16));
+      const float hi = bfr(bfr(__uint_as_float(w[e] & 0xFFFF0000u) * rn) * __uint_as_float(gw[e] & 0xFFFF0000u));
+      __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+      o[e] = *reinterpret_cast<uint32_t*>(&pr);
+    }
+    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // The packed greedy key of each row of fp32 logits (`cols` of them, vocabulary
 // ids id0 .. id0 + cols - 1 on this rank): float_key(max) << 32 | (2^32 - 1 -
 // id of the first maximum). The largest key over the ranks is the row's
