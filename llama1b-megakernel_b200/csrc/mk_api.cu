@@ -492,13 +492,17 @@ cudaError_t launch_gemm(const mk::GemmParams& gp, int tiles, int splits, cudaStr
 
 namespace {
 // Positions per attention CTA (a multiple of 32, at least 128 so each of the
-// 4 warps pipelines a chunk or more). The grid is batch x kv heads x splits
-// CTAs over 3 resident CTAs per SM, so the step takes about ceil(CTAs / (3
-// SMs)) waves of one split each: pick the length that minimises waves x
-// (length + the fixed cost of a CTA, ~64 positions' worth), the longer one
-// on ties. (A grid just over one wave, e.g. 512 CTAs of 1,024 positions at
-// bs 64, runs two waves, the second nearly empty.)
-int attn_split_len(int batch, int num_kv_heads, int max_len, int sms) {
+// 4 warps gets a chunk or more). The grid is batch x kv heads x splits CTAs
+// over 3 resident CTAs per SM, so the step takes about ceil(CTAs / (3 SMs))
+// waves of one split each: pick the length that minimises waves x (length +
+// the fixed cost of a CTA, in positions), the longer one on ties. The fixed
+// cost is what a CTA pays before its chunks stream: ~64 positions' worth for
+// the cp.async kernel (one chunk in flight per warp), ~512 for the TMA kernel
+// (measured: its 8-stage ring makes one long split per sequence and kv head
+// the fastest at bs 32 and 64; bs 64 1.94 -> 1.86 ms per step).
+constexpr int kAttnFixedCostCpAsync = 64;
+constexpr int kAttnFixedCostTma = 512;
+int attn_split_len(int batch, int num_kv_heads, int max_len, int sms, int fixed_cost) {
   const long long pairs = (long long)batch * num_kv_heads;
   const long long slots = 3LL * sms;
   const int hi = ((max_len + 31) / 32) * 32;
@@ -507,7 +511,7 @@ int attn_split_len(int batch, int num_kv_heads, int max_len, int sms) {
   for (int len = hi; len >= 128; len -= 32) {
     const long long splits = (max_len + len - 1) / len;
     const long long waves = (pairs * splits + slots - 1) / slots;
-    const long long cost = waves * (len + 64);
+    const long long cost = waves * (len + fixed_cost);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = len;
@@ -880,7 +884,8 @@ const char* mk_last_error(void) { return g_last_error.c_str(); }
 
 int64_t mk_paged_attention_workspace(int32_t batch, int32_t num_kv_heads, int32_t max_len) {
   if (batch < 1 || num_kv_heads < 1 || max_len < 1) return 0;
-  const int sl = attn_split_len(batch, num_kv_heads, max_len, device_sms());
+  // the workspace serves either kernel: the cp.async one's shorter splits are the most
+  const int sl = attn_split_len(batch, num_kv_heads, max_len, device_sms(), kAttnFixedCostCpAsync);
   const int64_t splits = (max_len + sl - 1) / sl;
   return (int64_t)batch * num_kv_heads * splits * 4 * mk::kAttnPartial * 4;
 }
@@ -914,21 +919,40 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
   ap.ps = page_size;
   ap.max_blocks = max_blocks;
   ap.num_pages = num_pages;
-  ap.split_len = attn_split_len(batch, num_kv_heads, max_len, device_sms());
+  ap.split_len = attn_split_len(batch, num_kv_heads, max_len, device_sms(),
+                                page_size % 32 == 0 ? kAttnFixedCostTma : kAttnFixedCostCpAsync);
   ap.splits = (max_len + ap.split_len - 1) / ap.split_len;
   ap.scale = scale;
   ap.work = static_cast<float*>(workspace);
   ap.out = static_cast<mk::bf16*>(out);
   ap.error = error;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  static bool attr = false;
-  if (!attr) {
-    MK_CUDA(cudaFuncSetAttribute(mk::paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 mk::kAttnSmem));
-    attr = true;
+  if (page_size % 32 == 0) {
+    // every 32-position chunk is one run of a page: TMA boxes into the staged ring
+    mk::PagedAttnTmaParams tp{};
+    tp.p = ap;
+    const long long pool_rows = (long long)num_pages * num_kv_heads * page_size;
+    if (pool_rows > 0x7fffffffLL) return fail(MK_EINVAL, "KV pool of %lld rows", pool_rows);
+    if (int rc = encode_sw128(&tp.tm_k, k_pages, pool_rows, 64, 32)) return rc;
+    if (int rc = encode_sw128(&tp.tm_v, v_pages, pool_rows, 64, 32)) return rc;
+    static bool tattr = false;
+    if (!tattr) {
+      MK_CUDA(cudaFuncSetAttribute(mk::paged_attn_tma_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, mk::kAttnTmaSmem));
+      tattr = true;
+    }
+    MK_CUDA(launch_pdl(mk::paged_attn_tma_kernel, dim3(ap.splits, num_kv_heads, batch),
+                       dim3((mk::kAttnCtaWarps + 1) * 32), mk::kAttnTmaSmem, st, tp));
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      MK_CUDA(cudaFuncSetAttribute(mk::paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   mk::kAttnSmem));
+      attr = true;
+    }
+    MK_CUDA(launch_pdl(mk::paged_attn_kernel, dim3(ap.splits, num_kv_heads, batch),
+                       dim3(mk::kAttnCtaWarps * 32), mk::kAttnSmem, st, ap));
   }
-  MK_CUDA(launch_pdl(mk::paged_attn_kernel, dim3(ap.splits, num_kv_heads, batch),
-                     dim3(mk::kAttnCtaWarps * 32), mk::kAttnSmem, st, ap));
   MK_CUDA(launch_pdl(mk::paged_attn_merge_kernel, dim3(num_kv_heads, batch), dim3(256), 0, st, ap));
   return MK_OK;
 }
