@@ -8,6 +8,7 @@
 //    the batch padded to 16, 32 or 64 with zero rows), both K-major with the
 //    128-byte swizzle (BP = 128 for prompt prefill: 128 token rows), loaded by 2-D
 //    TMA boxes of 64 columns (no multicast) into a ring of kGemmStages stages
+//    (kGemmStagesDeep when the launch puts at most one CTA on each SM)
 //    with full/empty mbarriers;
 //  * one lane issues tcgen05.mma (kind::f16, bf16 x bf16 -> fp32, M = 128,
 //    N = BP, K = 16; four per 64-column stage) into a TMEM accumulator of BP
@@ -34,7 +35,8 @@
 
 namespace mk {
 
-constexpr int kGemmStages = 4;  // 96 KB: two CTAs per SM overlap one tile's epilogue with the next's loads
+constexpr int kGemmStages = 4;      // 96 KB at 64 rows: two CTAs per SM overlap one tile's epilogue with the next's loads
+constexpr int kGemmStagesDeep = 8;  // a launch of at most one CTA per SM: twice the bytes in flight
 constexpr int kGemmTileN = 128;  // W rows per CTA (the MMA's M)
 constexpr int kGemmTileK = 64;   // columns per stage: one 128-byte swizzle atom per row
 constexpr int kGemmThreads = 128;
@@ -151,7 +153,7 @@ __device__ __forceinline__ void g_store(const GemmParams& p, size_t o, float y) 
   p.out[o] = __float2bfloat16_rn(y);
 }
 
-template <int BP>
+template <int BP, int kStages>
 __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) uint8_t gsm[];
   constexpr uint32_t kA = kGemmTileN * kGemmTileK * 2;  // 16 KB
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   static_assert(kStage % 1024 == 0, "stage buffers keep the 1024-byte swizzle alignment");
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(gsm);
   const uint32_t ring = (base + 1023) & ~1023u;
-  __shared__ __align__(8) uint64_t full[kGemmStages], empty[kGemmStages], done;
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], done;
   __shared__ uint32_t tmem_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -171,7 +173,7 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
   pdl_trigger();  // barrier init and TMEM allocation below overlap the previous kernel
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemmStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sa(&full[s])));
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sa(&empty[s])));
     }
@@ -195,8 +197,8 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
     // ---- producer: TMA boxes of W rows [tile*128, +128) and all X rows
     int issued = 0;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % kGemmStages;
-      if (i >= kGemmStages && !g_wait(p, sa(&empty[s]), ((i / kGemmStages) + 1) & 1, 101)) break;
+      const int s = i % kStages;
+      if (i >= kStages && !g_wait(p, sa(&empty[s]), ((i / kStages) + 1) & 1, 101)) break;
       const uint32_t a = ring + s * kStage, b = a + kA;
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(&full[s])),
                    "r"(kStage)
@@ -206,9 +208,9 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
       ++issued;
     }
     // every box issued lands before the CTA may exit (bounded)
-    for (int i = (issued > kGemmStages ? issued - kGemmStages : 0); i < issued; ++i) {
-      const int s = i % kGemmStages;
-      const uint32_t par = (i / kGemmStages) & 1;
+    for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i) {
+      const int s = i % kStages;
+      const uint32_t par = (i / kStages) & 1;
       const uint64_t t0 = g_now();
       while (!g_try_wait(sa(&full[s]), par) && g_now() - t0 < 2 * p.timeout_ns) {
       }
@@ -218,8 +220,8 @@ __global__ void __launch_bounds__(kGemmThreads) gemm_kernel(const __grid_constan
     constexpr uint32_t idesc = gemm_idesc<BP>();
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
-      const int s = i % kGemmStages;
-      if (!g_wait(p, sa(&full[s]), (i / kGemmStages) & 1, 102)) {
+      const int s = i % kStages;
+      if (!g_wait(p, sa(&full[s]), (i / kStages) & 1, 102)) {
         ok = false;
         break;
       }
