@@ -94,3 +94,14 @@ def test_tp8_one_kv_head_per_gpu(tmp_path):
     assert r["ids_match"] >= 0.95, r
     assert r["generate_self_consistent"], r
     _check_oracle_and_batched(r)
+
+
+@pytest.mark.skipif(_gpus() < 4, reason="needs 4 GPUs")
+def test_tp4_two_kv_heads_per_gpu(tmp_path):
+    """Four ranks: the peer exchanges sum four partials in rank order."""
+    r = _run(4, "mid", tmp_path)
+    assert r["kv_layer0_exact"], r
+    assert r["cos_min"] >= 0.9999 and r["maxabs_max"] <= 5e-2, r
+    assert r["ids_match"] >= 0.95, r
+    assert r["generate_self_consistent"], r
+    _check_oracle_and_batched(r)
