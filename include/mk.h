@@ -132,6 +132,20 @@ int mk_decode(MkModel* m, const int32_t* tokens, const int32_t* positions, int32
               void* stream);
 
 /*
+ * mk_decode with HOST buffers, synchronous: copies tokens[batch] and
+ * positions[batch] (int32, host) to the device, enqueues the step on
+ * `stream`, copies the greedy ids back into next_ids[batch] (int32, host),
+ * waits for the stream and reports device errors as mk_sync does. logits is a
+ * device pointer as in mk_decode (may be NULL). The staging buffers are the
+ * handle's own (allocated by mk_init), so calls on one handle must not
+ * overlap. This is one token-generation call of the reference's model
+ * forward (`llama_with_megakernel.py:165-173` inside NxDI's decode step) with
+ * its host-side inputs and output.
+ */
+int mk_decode_host(MkModel* m, const int32_t* tokens, const int32_t* positions, int32_t batch,
+                   const MkKVCache* kv, float* logits, int32_t* next_ids, void* stream);
+
+/*
  * The decoder layers only, the role of the reference's 16-layer kernel:
  * hidden_in [batch][hidden] bf16 (the embedded token) -> hidden_out
  * [batch][hidden] bf16 (the residual after the last layer, before the final

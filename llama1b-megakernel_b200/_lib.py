@@ -22,7 +22,8 @@ STATUS_NAMES = {
 
 # Every symbol include/mk.h declares (checked by tests/test_abi.py).
 EXPORTED = (
-    "mk_init", "mk_load_weights", "mk_decode", "mk_decode_static", "mk_decode_hidden", "mk_sync",
+    "mk_init", "mk_load_weights", "mk_decode", "mk_decode_host", "mk_decode_static", "mk_decode_hidden",
+    "mk_sync",
     "mk_set_timeout_ns", "mk_debug_skip_arrival", "mk_set_trace",
     "mk_query", "mk_schedule_gap", "mk_sample", "mk_paged_attention_workspace",
     "mk_paged_attention", "mk_gemm_workspace", "mk_gemm_bf16", "mk_rmsnorm_rows", "mk_rope_scatter", "mk_swiglu", "mk_argmax_rows",
@@ -90,6 +91,7 @@ def load() -> ctypes.CDLL:
     lib.mk_init.argtypes = [P(MkConfig), ctypes.c_int, P(VP)]
     lib.mk_load_weights.argtypes = [VP, P(MkWeights)]
     lib.mk_decode.argtypes = [VP, VP, VP, I32, P(MkKVCache), VP, VP, I32, VP]
+    lib.mk_decode_host.argtypes = [VP, VP, VP, I32, P(MkKVCache), VP, VP, VP]
     lib.mk_decode_static.argtypes = [P(MkConfig), P(MkWeights), VP, VP, I32, P(MkKVCache), VP, VP,
                                      I32, VP, VP]
     lib.mk_decode_hidden.argtypes = [VP, VP, VP, I32, P(MkKVCache), VP, VP]

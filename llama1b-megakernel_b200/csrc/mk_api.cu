@@ -83,6 +83,9 @@ struct MkModel {
   int* error = nullptr;
   int* host_error = nullptr;      // mapped pinned mirror, read by mk_sync
   int* host_error_dev = nullptr;  // its device address
+  // mk_decode_host staging: tokens, positions, next ids ([3][max_batch] int32)
+  int32_t* io_dev = nullptr;   // in the scratch allocation
+  int32_t* io_host = nullptr;  // pinned
   size_t counters_bytes = 0;
   unsigned long long* trace = nullptr;  // borrowed, see mk_set_trace
   // tensor parallelism (mk_tp_setup / mk_tp_connect)
@@ -639,6 +642,7 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   const size_t o_keys = take(B * 8);
   const size_t o_err = take(16);
   m->counters_bytes = o_err + 256 - o_cnt;  // counters, keys and error word
+  const size_t o_io = take((size_t)3 * B * 4);
   void* base = nullptr;
   e = cudaMalloc(&base, off);
   if (e != cudaSuccess) {
@@ -658,7 +662,9 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   m->counters = reinterpret_cast<uint32_t*>(cb + o_cnt);
   m->keys = reinterpret_cast<unsigned long long*>(cb + o_keys);
   m->error = reinterpret_cast<int*>(cb + o_err);
+  m->io_dev = reinterpret_cast<int32_t*>(cb + o_io);
   e = cudaMemset(base, 0, off);
+  if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&m->io_host), (size_t)3 * B * 4, cudaHostAllocDefault);
   if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void**>(&m->host_error), 16, cudaHostAllocMapped);
   if (e == cudaSuccess) {
     memset(m->host_error, 0, 16);
@@ -667,6 +673,7 @@ int mk_init(const MkConfig* cfg, int device, MkModel** out) {
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (m->host_error) cudaFreeHost(m->host_error);
+    if (m->io_host) cudaFreeHost(m->io_host);
     cudaFree(base);
     delete m;
     return fail(MK_ECUDA, "scratch init: %s", cudaGetErrorString(e));
@@ -694,6 +701,28 @@ int mk_decode(MkModel* m, const int32_t* tokens, const int32_t* positions, int32
               const MkKVCache* kv, float* logits, int32_t* next_ids, int32_t flags, void* stream) {
   return enqueue(m, 0, tokens, positions, batch, kv, nullptr, nullptr, logits, next_ids, flags,
                  stream);
+}
+
+int mk_decode_host(MkModel* m, const int32_t* tokens, const int32_t* positions, int32_t batch,
+                   const MkKVCache* kv, float* logits, int32_t* next_ids, void* stream) {
+  if (!m) return fail(MK_EINVAL, "model is NULL");
+  if (!tokens || !positions || !next_ids) return fail(MK_EINVAL, "tokens, positions and next_ids are required");
+  if (batch < 1 || batch > m->cfg.max_batch)
+    return fail(MK_EINVAL, "batch %d outside [1, max_batch=%d]", batch, m->cfg.max_batch);
+  MK_CUDA(cudaSetDevice(m->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* in_h = m->io_host;
+  memcpy(in_h, tokens, (size_t)batch * 4);
+  memcpy(in_h + batch, positions, (size_t)batch * 4);
+  MK_CUDA(cudaMemcpyAsync(m->io_dev, in_h, (size_t)2 * batch * 4, cudaMemcpyHostToDevice, st));
+  if (int rc = enqueue(m, 0, m->io_dev, m->io_dev + batch, batch, kv, nullptr, nullptr, logits,
+                       m->io_dev + 2 * batch, 0, stream))
+    return rc;
+  MK_CUDA(cudaMemcpyAsync(in_h + 2 * batch, m->io_dev + 2 * batch, (size_t)batch * 4,
+                          cudaMemcpyDeviceToHost, st));
+  if (int rc = mk_sync(m, stream)) return rc;
+  memcpy(next_ids, in_h + 2 * batch, (size_t)batch * 4);
+  return MK_OK;
 }
 
 int mk_decode_static(const MkConfig* cfg, const MkWeights* w, const int32_t* tokens,
@@ -1299,6 +1328,7 @@ int mk_destroy(MkModel* m) {
   if (m->xbuf) cudaFree(m->xbuf);
   if (m->scratch) cudaFree(m->scratch);
   if (m->host_error) cudaFreeHost(m->host_error);
+  if (m->io_host) cudaFreeHost(m->io_host);
   delete m;
   return MK_OK;
 }

@@ -17,6 +17,7 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -55,10 +56,12 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
             self._tokens = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
             self._positions = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
             self._next = torch.zeros(max_batch, dtype=torch.int32, device=self.device)
-            # pinned staging for forward(): token + position in, next id out
-            self._h_in = torch.zeros(2, max_batch, dtype=torch.int32).pin_memory()
-            self._d_in = torch.zeros(2, max_batch, dtype=torch.int32, device=self.device)
-            self._h_next = torch.zeros(max_batch, dtype=torch.int32).pin_memory()
+            # host staging for forward()'s single-position calls (mk_decode_host
+            # copies through the handle's own pinned buffer)
+            self._h_in = np.zeros((2, max_batch), dtype=np.int32)
+            self._h_next = np.zeros(max_batch, dtype=np.int32)
+            self._h_addr = (self._h_in[0].ctypes.data, self._h_in[1].ctypes.data,
+                            self._h_next.ctypes.data)
             # lm_head rows this model scores (a tensor-parallel rank scores a slice)
             self.lm_rows = lm_rows or cfg.vocab
             self._logits = torch.empty(max_batch, self.lm_rows, dtype=torch.float32,
@@ -172,7 +175,6 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         _lib.check(self.lib.mk_sync(self._handle, self._stream_ptr(stream)))
 
     # ------------------------------------------------------------ model API
-    @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, position_ids: torch.Tensor | None = None,
                 past_key_values: PagedKVCache | None = None, return_logits: bool = True,
                 sync: bool = True) -> DecodeOutput:
@@ -185,6 +187,44 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         synchronised; the device tensor with ``sync=False``) and the cache.
         """
         kv = past_key_values if past_key_values is not None else self.kv
+        if (sync and position_ids is not None and type(input_ids) is torch.Tensor
+                and type(position_ids) is torch.Tensor and input_ids.device.type == "cpu"
+                and position_ids.device.type == "cpu"):
+            n = input_ids.numel()
+            if (n == position_ids.numel() and n <= self.max_batch
+                    and (input_ids.dim() == 2 and input_ids.shape[1] == 1
+                         or input_ids.dim() == 1 and n == 1)):
+                return self._step_host(input_ids, position_ids, kv, return_logits)
+        return self._forward(input_ids, position_ids, kv, return_logits, sync)
+
+    def _step_host(self, input_ids: torch.Tensor, position_ids: torch.Tensor, kv: PagedKVCache,
+                   return_logits: bool) -> DecodeOutput:
+        """One position of B sequences from host tensors: the numbers go through
+        numpy into the staging arrays and one C call (mk_decode_host) copies
+        them in, launches, copies the greedy ids out and synchronises, so the
+        step's host work is a handful of Python operations."""
+        h = self._h_in
+        B = input_ids.numel()
+        h[0, :B] = input_ids.numpy().reshape(-1)
+        h[1, :B] = position_ids.numpy().reshape(-1)
+        lens = kv.seq_lens
+        for b in range(B):
+            p = int(h[1, b]) + 1
+            kv.reserve(b, p)
+            if p > lens[b]:
+                lens[b] = p
+        logits = self._logits[:B] if return_logits else None
+        a_tok, a_pos, a_next = self._h_addr
+        _lib.check(self.lib.mk_decode_host(
+            self._handle, a_tok, a_pos, B, ctypes.byref(self._kv_struct(kv)),
+            logits.data_ptr() if logits is not None else None, a_next,
+            torch.cuda.current_stream(self.device).cuda_stream))
+        return DecodeOutput(logits.clone() if logits is not None else None,
+                            torch.from_numpy(self._h_next[:B].astype(np.int64)), kv)
+
+    @torch.no_grad()
+    def _forward(self, input_ids, position_ids, kv: PagedKVCache, return_logits: bool,
+                 sync: bool) -> DecodeOutput:
         ids = torch.as_tensor(input_ids)
         if ids.dim() == 1:
             ids = ids[None, :]
@@ -200,28 +240,20 @@ class MegakernelLlamaForCausalLM(torch.nn.Module):
         for b in range(B):
             kv.reserve(b, last[b] + 1)
         logits = self._logits[:B] if return_logits else None
-        if T == 1 and sync and ids.device.type == "cpu":
-            # one pinned staging buffer, one H2D copy for token and position
-            # (reused by the next call, so only when this call synchronises)
-            self._h_in[0, :B].copy_(ids[:, 0])
-            self._h_in[1, :B].copy_(pos_host[:, 0])
-            self._d_in[:, :B].copy_(self._h_in[:, :B], non_blocking=True)
-            self.launch(self._d_in[0, :B], self._d_in[1, :B], kv, logits, self._next[:B])
-        else:
-            ids_dev = ids.to(device=self.device, dtype=torch.int32, non_blocking=True)
-            pos_dev = pos.to(device=self.device, dtype=torch.int32, non_blocking=True)
-            for t in range(T):
-                self.launch(ids_dev[:, t].contiguous(), pos_dev[:, t].contiguous(), kv,
-                            logits if t == T - 1 else None, self._next[:B])
+        ids_dev = ids.to(device=self.device, dtype=torch.int32, non_blocking=True)
+        pos_dev = pos.to(device=self.device, dtype=torch.int32, non_blocking=True)
+        for t in range(T):
+            self.launch(ids_dev[:, t].contiguous(), pos_dev[:, t].contiguous(), kv,
+                        logits if t == T - 1 else None, self._next[:B])
         for b in range(B):
             if last[b] + 1 > kv.seq_lens[b]:
                 kv.seq_lens[b] = last[b] + 1
         if not sync:
             return DecodeOutput(logits, self._next[:B].to(torch.int64), kv)
-        self._h_next[:B].copy_(self._next[:B], non_blocking=True)
+        nxt = self._next[:B].cpu()  # waits for the stream
         self.sync()
         return DecodeOutput(logits.clone() if logits is not None else None,
-                            self._h_next[:B].to(torch.int64), kv)
+                            nxt.to(torch.int64), kv)
 
     def sample(self, logits: torch.Tensor, top_k: int = 1, top_p: float = 1.0,
                temperature: float = 1.0, seed: int = 0, step: int = 0,
