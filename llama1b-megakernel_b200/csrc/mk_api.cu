@@ -998,7 +998,9 @@ int mk_paged_attention(const void* q, const void* k_pages, const void* v_pages,
     MK_CUDA(launch_pdl(mk::paged_attn_kernel, dim3(ap.splits, num_kv_heads, batch),
                        dim3(mk::kAttnCtaWarps * 32), mk::kAttnSmem, st, ap));
   }
-  MK_CUDA(launch_pdl(mk::paged_attn_merge_kernel, dim3(num_kv_heads, batch), dim3(256), 0, st, ap));
+  // a single split writes its heads' output itself
+  if (ap.splits > 1)
+    MK_CUDA(launch_pdl(mk::paged_attn_merge_kernel, dim3(num_kv_heads, batch), dim3(256), 0, st, ap));
   return MK_OK;
 }
 

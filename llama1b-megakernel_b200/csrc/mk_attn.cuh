@@ -22,7 +22,8 @@
 //    memory, and the CTA writes one (m, l, o[64]) partial per head;
 //  * a merge kernel (one CTA per sequence and kv head) combines the splits and
 //    writes o as bf16, the rounding of the attention output the single-GPU
-//    kernel uses.
+//    kernel uses; with a single split the CTA writes o itself and the merge
+//    kernel is not launched.
 // Positions index pages through the block table; a page id outside the pool
 // sets the error word and the position is skipped (never dereferenced).
 #pragma once
@@ -189,6 +190,12 @@ __device__ __forceinline__ void attn_write_partial(const PagedAttnParams& p,
       const float a = (st[w][hh][0] == -INFINITY) ? 0.f : __expf(st[w][hh][0] - M);
       L += st[w][hh][1] * a;
       O += st[w][hh][2 + d] * a;
+    }
+    if (p.splits == 1) {
+      // the only split: the merge kernel would scale by exp(0) = 1, so write
+      // the normalised output here and skip it
+      p.out[((size_t)b * p.NQ + g * 4 + hh) * 64 + d] = __float2bfloat16_rn(L > 0.f ? O / L : 0.f);
+      continue;
     }
     if (d == 0) {
       dst[hh * kAttnPartial + 0] = M;
