@@ -461,7 +461,13 @@ def run_ours(args, ws, rank, local):
         batched_res = run_batched(model, cfg, dev, hbm_peak)
     tp_bs32 = None
     if tp_world > 1 and not (args.no_batched or args.small):
-        tp_bs32 = run_tp_batched(model, cfg, dev, ws)
+        # an extra: a failure is reported in the line rather than losing the headline (the
+        # same code runs on every rank, so a failure is expected on all of them alike)
+        try:
+            tp_bs32 = run_tp_batched(model, cfg, dev, ws)
+        except Exception as e:  # noqa: BLE001
+            tp_bs32 = {"error": f"{type(e).__name__}: {e}"[:300]}
+            torch.cuda.empty_cache()
 
     # ------------------------------------------------------------ cpu baseline (config 1)
     cpu_b = None
