@@ -79,14 +79,16 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--small", action="store_true",
                     help="profiling case: a few steps, no e2e / sweep / cpu baseline")
-    ap.add_argument("--case", choices=["small4", "gemm", "batched", "trace"], default=None,
+    ap.add_argument("--case", choices=["small4", "gemm", "batched", "trace", "attn"], default=None,
                     help="ncu profiling cases (print timings, no JSON line): small4 - 4 "
                          "Llama-3.2-1B layers, vocab 32000, one step at ctx 512 after 4 warm-up "
                          "steps; gemm - the tcgen05 GEMM on the batched projection shapes at 8 "
                          "and 64 rows (3 warm-up + 7 timed launches each, L2 flushed, cuBLAS "
                          "beside it); batched - one bs-64 batched step at KV 1024 replayed "
                          "inside the NVTX range 'replay'; trace - the per-phase trace of "
-                         "Llama-3.2-1B steps at ctx 1024 (mk_set_trace, summarised by trace.py)")
+                         "Llama-3.2-1B steps at ctx 1024 (mk_set_trace, summarised by trace.py); "
+                         "attn - the batched paged attention alone, bs 64 x 4096 cached positions "
+                         "of one layer (536 MB of K/V), 3 warm-up and 5 timed launches")
     return ap.parse_args()
 
 
@@ -637,6 +639,51 @@ def run_case_gemm():
             del w
 
 
+def run_case_attn():
+    """mk_paged_attention alone on one layer of the bs-64 batched step, at 4096
+    cached positions per sequence (K/V 536 MB, larger than L2), page size 64:
+    the TMA kernel. Prints the median launch time and the K/V bytes per second."""
+    import ctypes
+
+    from llama1b_megakernel_b200 import _lib
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    B, NKV, NQ, L, PS = 64, 8, 32, 4096, 64
+    blocks = L // PS + 1
+    pages = B * blocks
+    k = (torch.randn(pages, NKV, PS, 64, device=dev) * 0.5).bfloat16()
+    v = torch.randn(pages, NKV, PS, 64, device=dev).bfloat16()
+    table = torch.randperm(pages, device=dev, dtype=torch.int32).reshape(B, blocks).contiguous()
+    lengths = torch.full((B,), L, dtype=torch.int32, device=dev)
+    q = torch.randn(B, NQ, 64, device=dev).bfloat16()
+    out = torch.empty(B, NQ, 64, dtype=torch.bfloat16, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = lib.mk_paged_attention_workspace(B, NKV, L)
+    work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+
+    def run():
+        _lib.check(lib.mk_paged_attention(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), table.data_ptr(), lengths.data_ptr(), B, NQ,
+            NKV, PS, blocks, pages, L, ctypes.c_float(0.125), work.data_ptr(), work.numel(),
+            out.data_ptr(), err.data_ptr(), torch.cuda.current_stream().cuda_stream))
+
+    for _ in range(3):
+        run()
+    ts = []
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    t = statistics.median(ts)
+    kv_bytes = B * NKV * L * 64 * 2 * 2
+    print(f"paged attention bs {B} x {L} positions: {t * 1e3:.1f} us, "
+          f"{kv_bytes / t / 1e6:.0f} GB/s of K/V, error word {int(err)}")
+
+
 def run_case_batched():
     """One bs-64 batched step at KV 1024, replayed once inside NVTX 'replay'."""
     from llama1b_megakernel_b200 import synthetic as syn
@@ -755,6 +802,9 @@ def main():
         return
     if args.case == "batched":
         run_case_batched()
+        return
+    if args.case == "attn":
+        run_case_attn()
         return
     ws, rank, local = dist_init()
     try:
