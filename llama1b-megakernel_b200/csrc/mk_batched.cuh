@@ -297,13 +297,12 @@ __global__ void __launch_bounds__(256) xreduce_add_rmsnorm_kernel(const __grid_c
   pdl_trigger();
   pdl_wait();
   __shared__ float red[8];
-  __shared__ int bad;
   const int b = blockIdx.x, tid = threadIdx.x, H = p.H, W = p.W;
   const int slot = p.exchange % kXchgSlots;
   const unsigned long long tag =
       (unsigned long long)p.epoch[0] * kXchgPerStep + (unsigned long long)p.exchange + 1ull;
   const size_t foff = xchg_flags_offset(p.rows, H) / 8 + (size_t)slot * kMaxTp;  // in u64 words
-  if (tid == 0) bad = 0;
+  int timed_out = 0;
   // Block 0 posts this rank's flag on every rank (the GEMM that wrote the
   // partial finished before this grid started).
   if (b == 0 && tid < W) {
@@ -325,14 +324,13 @@ __global__ void __launch_bounds__(256) xreduce_add_rmsnorm_kernel(const __grid_c
           t0 = now;
         } else if (now - t0 > p.timeout_ns) {
           atomicCAS(p.error, 0, 3);
-          bad = 1;
+          timed_out = 1;
           break;
         }
       }
     }
   }
-  __syncthreads();
-  if (bad) return;
+  if (__syncthreads_or(timed_out)) return;
   uint4* xr = reinterpret_cast<uint4*>(p.x + (size_t)b * H);
   float ss = 0.f;
   for (int i = tid; i < H / 8; i += 256) {
