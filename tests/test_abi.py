@@ -70,3 +70,25 @@ def test_check_raises_with_message(lib):
     lib.mk_sync(None, None)
     with pytest.raises(_lib.MkError, match="MK_EINVAL"):
         _lib.check(_lib.MK_EINVAL)
+
+
+def test_exchange_buffer_layout(lib):
+    """Two fp32 [rows][hidden] slots, then the flag words at the next 256-byte
+    boundary: 2 slots x 8 ranks of 64-bit words."""
+    for rows, hidden in ((1, 8), (32, 2048), (3, 264)):
+        slots = 2 * rows * hidden * 4
+        flags_at = (slots + 255) // 256 * 256
+        assert lib.mk_xbuf_bytes(rows, hidden) == flags_at + 2 * 8 * 8
+    assert lib.mk_xbuf_bytes(0, 2048) == 0 and lib.mk_xbuf_bytes(4, 12) == 0
+
+
+def test_host_entry_points_reject_bad_arguments_without_cuda(lib):
+    kv = _lib.MkKVCache()
+    tok = (ctypes.c_int32 * 1)(0)
+    assert lib.mk_decode_host(None, tok, tok, 1, ctypes.byref(kv), None, tok, None) == _lib.MK_EINVAL
+    assert lib.mk_allreduce_add_rmsnorm(None, 0, 2, 1, 0, None, None, None, ctypes.c_float(1e-5),
+                                        1, 8, None, None, 0, None) == _lib.MK_EINVAL
+    assert lib.mk_step_epoch(None, None) == _lib.MK_EINVAL
+    assert lib.mk_xbuf_alloc(0, None, None) == _lib.MK_EINVAL
+    assert lib.mk_xbuf_open(None, None) == _lib.MK_EINVAL
+    assert lib.mk_xbuf_close(None) == _lib.MK_OK and lib.mk_xbuf_free(None) == _lib.MK_OK
